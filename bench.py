@@ -1,0 +1,341 @@
+"""Benchmark of the fused optimizer step (ZeRO-1 DP).
+
+Workload: 200M parameters, bf16 params and bf16 grads (N(0,1e-3) x loss scale
+65536, seeded per rank), fp32 master/m/v, 25M-element gradient buckets,
+global-norm clip 1.0, dynamic loss scaler, lr 1e-3, wd 0.01. At N GPUs each
+rank brings its own full 200M-element gradient; a step reduce-scatters it
+(NCCL, avg), runs the fused unscale/norm/clip/AdamW on the rank's 1/N shard and
+all-gathers the bf16 params. Unit: one parameter-gradient of one rank reduced
+and applied, so per-GPU work is fixed as N grows ("weak"); at N = 1 it is
+simply parameters updated per second.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Rank 0 prints one JSON line. `--impl reference` times the reference's own CPU
+AdamW (oracle/_ref: the unmodified src/optim/adamw.cpp; the port oracle if that
+was not built) on a bounded sample of the same workload with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT / "soar.cpp_b200", ROOT):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+N_PARAMS = 200_000_000
+BUCKET = 25_000_000
+BYTES_PER_PARAM = 28          # algorithmic: read g 2 + master/m/v 12, write master/m/v 12 + param 2
+METRIC = "AdamW Gparams/s (fused ZeRO-1 optimizer step, 200M bf16-mixed params)"
+UNIT = "Gparams/s"
+# dram__bytes_read.sum + dram__bytes_write.sum of one k_apply launch on the full
+# 200M workload, from the ncu capture summarised in profiles/ (None until captured).
+APPLY_TRAFFIC_BYTES = None
+
+
+def measured_peak_hbm() -> tuple[float, str]:
+    try:
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--params", type=int, default=N_PARAMS)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------ CPU baseline --
+
+def cpu_reference_sample(n: int, steps: int, warmup: int = 1) -> dict:
+    """The reference's clip_grad_norm(1.0) + step() (adamw.cpp:87-176) on one
+    fp32 bucket of n params (the unscaled grads and fp32 master of the mixed
+    workload), OpenMP over all host threads. Returns Gparams/s."""
+    import numpy as np
+
+    from oracle import oracle
+    from soar_b200 import synth
+    threads = os.cpu_count() or 1
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    p = synth.normal(synth.seed_of(4, 0), n, 0.02)
+    g = synth.normal(synth.seed_of(4, 1, 0), n, 1e-3)
+    if oracle.ref_available():
+        opt = oracle.RefAdamW([p], [g], lr=1e-3, weight_decay=0.01)
+        kind = "reference"
+
+        def one():
+            opt.clip_grad_norm(1.0)
+            opt.step()
+    else:
+        cfg = oracle.StepConfig(layout=0, max_norm=1.0)
+        opt = oracle.PortOptimizer([p], [0.01], cfg)
+        kind = "port"
+
+        def one():
+            opt.step([g])
+    for _ in range(warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    dt = time.perf_counter() - t0
+    return {"value": n * steps / dt / 1e9, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{steps} steps of clip_grad_norm(1.0)+step() on one fp32 bucket of "
+                      f"{n} params (host arrays, unscale/bf16 cast not timed)",
+            "ms_per_step": dt / steps * 1e3}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    n = min(BUCKET, args.params)
+    t0 = time.perf_counter()
+    res = cpu_reference_sample(n, args.steps, args.warmup)
+    line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config4 sample: one 25M bucket, fp32 reference AdamW",
+                       "params": n},
+            "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "wall_s": time.perf_counter() - t0}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ clocks --
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, path: Path):
+        self.path = path
+        self.proc = None
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self, gpus: list[int]) -> dict | None:
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9 or not f[0].isdigit() or int(f[0]) not in gpus:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- our arm --
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    import soar_b200 as sb
+    from soar_b200 import dp, synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    comm = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        comm = dp.TorchComm()
+    n = args.params
+    dev = torch.device("cuda", local)
+
+    # params: identical on every rank; grads: per rank
+    p_host = synth.to_bf16_bits(synth.normal(synth.seed_of(4, 0), n, 0.02))
+    g_host = synth.to_bf16_bits(synth.normal(synth.seed_of(4, 1, 0, rank), n, 1e-3)
+                                * np.float32(65536.0))
+    params = torch.from_numpy(p_host.view(np.int16)).view(torch.bfloat16).to(dev)
+    grads = torch.from_numpy(g_host.view(np.int16)).view(torch.bfloat16).to(dev)
+
+    def make_opt(sp, sg):
+        return sb.AdamW([sb.ParamGroup(sp, 0.01)], sb.AdamWOptions(lr=1e-3, weight_decay=0.01),
+                        layout="bf16_mixed", max_grad_norm=1.0,
+                        loss_scaler=sb.LossScalerOptions(init_scale=65536.0), grads=sg,
+                        device=local)
+
+    z = dp.ZeroOneAdamW(params, grads, BUCKET, make_opt, comm)
+    stream = torch.cuda.current_stream()
+    shard_params = sum(b.own_size for b in z.buckets)
+
+    def barrier():
+        if comm:
+            torch.distributed.barrier(device_ids=[local])
+
+    def one_step(ev=None):
+        z.reduce_scatter()
+        parts = z.norm_partials()
+        if ev is not None:
+            ev[0].record(stream)
+        z.update(parts)
+        if ev is not None:
+            ev[1].record(stream)
+        z.all_gather()
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(ROOT / "gpurun_out" / f"clocks_rank{rank}.csv") if rank == 0 else None
+    if clocks:
+        (ROOT / "gpurun_out").mkdir(exist_ok=True)
+        clocks.start()
+        time.sleep(0.3)
+    apply_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for k in range(args.steps):
+        one_step(apply_ev[k])
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clock_info = clocks.stop(list(range(world))) if clocks else None
+
+    ms = start.elapsed_time(end)
+    apply_ms = [a.elapsed_time(b) for a, b in apply_ev]
+    t = torch.tensor([ms, statistics.mean(apply_ms)], dtype=torch.float64, device=dev)
+    if comm:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms_max, apply_ms_max = float(t[0]), float(t[1])
+    info = z.opt.info()
+
+    # ---- end to end through the public API with host buffers -------------
+    g_pin = torch.from_numpy(g_host.view(np.int16)).view(torch.bfloat16).pin_memory()
+    p_pin = torch.empty(n, dtype=torch.bfloat16).pin_memory()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        grads.copy_(g_pin, non_blocking=True)
+        z.step()
+        p_pin.copy_(params, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    if comm:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    e2e_ms = float(t[0])
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            cpu = cpu_reference_sample(min(BUCKET, n), 5)
+            cpu.pop("ms_per_step", None)
+        except Exception as ex:  # the baseline is reported, never required
+            cpu = {"error": str(ex)}
+
+    if comm:
+        torch.distributed.barrier(device_ids=[local])
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return 0
+    peak, peak_kind = measured_peak_hbm()
+    apply_bytes = BYTES_PER_PARAM * shard_params
+    achieved = apply_bytes / (apply_ms_max * 1e-3) / 1e9
+    units = world * n * args.steps
+    line = {
+        "metric": METRIC,
+        "value": units / (ms_max * 1e-3) / 1e9,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_max / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": "config4: ZeRO-1 fused AdamW step, 200M params bf16 params+grads, "
+                               "fp32 master/m/v, 25M buckets, clip 1.0, loss scaler 65536",
+                   "params": n, "bucket": BUCKET, "params_per_rank_shard": shard_params,
+                   "parallelism": f"dp{world} zero1", "global_batch": None, "seq_len": None,
+                   "l2": "inputs larger than L2 (16 B/param resident state = "
+                         f"{16 * shard_params / 1e9:.1f} GB per rank)"},
+        "roofline": {"bound": "hbm", "kernel": "k_apply", "achieved": achieved, "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": APPLY_TRAFFIC_BYTES,
+                     "algorithmic_bytes_per_launch": apply_bytes,
+                     "apply_ms": apply_ms_max},
+        "cpu_baseline": cpu,
+        "e2e": {"value": world * n * args.e2e_steps / (e2e_ms * 1e-3) / 1e9, "unit": UNIT,
+                "h2d_bytes_per_step": 2 * n, "d2h_bytes_per_step": 2 * n,
+                "ms_per_step": e2e_ms / args.e2e_steps},
+        "clocks": clock_info,
+        "gpu_launches": 2 * args.steps,
+        "final_info": {"step": info.step, "skipped": info.skipped, "loss_scale": info.loss_scale,
+                       "grad_norm": info.grad_norm},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,195 @@
+/*
+ * soar_optim.h -- C-ABI of the B200 (sm_100a) optimizer-step hot path.
+ *
+ * Drop-in for the update step of pomagrenate/soar.cpp: the reference's
+ * soar::optim::AdamW / CosineAnnealingLR (include/soar/optim/adamw.hpp:10-57,
+ * src/optim/adamw.cpp:66-202), which the Trainer calls as
+ * clip_grad_norm(grad_clip) -> step() -> zero_grad()
+ * (src/engine/trainer.cpp:157-159, 223-225). The reference exposes its engine
+ * through an opaque-handle C-ABI (include/soar/api/c_api.h) bound from Python
+ * with ctypes (soar/__init__.py:48-95); these entry points follow the same
+ * conventions and are additive to it:
+ *   - SOAR_API = default visibility (c_api.h:10-14);
+ *   - opaque void* handles; int status, 0 = success, -1 = any failure or NULL
+ *     argument (src/api/c_api.cpp:82-84, 100, 129, 148);
+ *   - caller-owned out-pointers;
+ *   - plus a `void* stream` (a cudaStream_t; NULL = legacy default stream), the
+ *     convention of the reference's kernel API (include/soar/cuda/cuda_kernels.hpp:108-127).
+ * soar_last_error() returns the message of the calling thread's last failure.
+ *
+ * Memory: parameters and gradients are caller-owned device buffers (the model
+ * owns its params, as in the reference where AdamW copies the TensorPtr list,
+ * adamw.hpp:33). The optimizer owns its state -- fp32 master weights (mixed
+ * layout), first and second moments -- in one device slab it allocates at
+ * create time, as the reference's AdamW owns m_/v_ (adamw.hpp:38-39).
+ *
+ * No entry point synchronises the host except those documented as
+ * synchronous (clip_grad_norm returns a value, as in the reference, and the
+ * state readers copy to host memory).
+ */
+#ifndef SOAR_OPTIM_H
+#define SOAR_OPTIM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define SOAR_API __declspec(dllexport)
+#else
+#define SOAR_API __attribute__((visibility("default")))
+#endif
+
+#define SOAR_OK 0
+#define SOAR_ERROR (-1)
+
+/* Storage layouts. 28 algorithmic bytes per parameter per step in both. */
+enum soar_layout {
+    /* fp32 params (updated in place, they are the master), fp32 grads, fp32 m/v:
+       the reference's only layout (adamw.cpp:143-147). */
+    SOAR_LAYOUT_FP32 = 0,
+    /* bf16 params and grads, fp32 master/m/v owned by the optimizer; params are
+       rewritten as round-to-nearest-even bf16 of the master every step. */
+    SOAR_LAYOUT_BF16_MIXED = 1
+};
+
+/* Which optimizer-owned state array of a tensor (soar_optim_state_ptr & co). */
+enum soar_state_kind { SOAR_STATE_MASTER = 0, SOAR_STATE_M = 1, SOAR_STATE_V = 2 };
+
+/* One parameter tensor (the reference's TensorPtr list entry). */
+typedef struct soar_tensor_desc {
+    void* param;        /* device; fp32 (FP32 layout) or bf16 (BF16_MIXED) */
+    void* grad;         /* device, same dtype as param. NULL: the tensor is skipped by
+                           step/clip, as a param without grad is (adamw.cpp:89-90,133-134) */
+    uint64_t numel;
+    float weight_decay; /* this tensor's decoupled weight decay (per-param-group mask) */
+} soar_tensor_desc;
+
+/* Optimizer options. The first five fields are the reference's AdamWOptions
+   (adamw.hpp:10-16, same defaults); the rest are extensions with no reference
+   counterpart. Fill with soar_adamw_default_opts() first. */
+typedef struct soar_adamw_opts {
+    float lr;               /* 1e-3 */
+    float beta1;            /* 0.9 */
+    float beta2;            /* 0.999 */
+    float eps;              /* 1e-8 */
+    float weight_decay;     /* 1e-2: used by soar_optim_create_uniform; create() takes
+                               each tensor's own weight_decay */
+    int32_t layout;         /* enum soar_layout, default FP32 */
+    float max_grad_norm;    /* > 0: step() clips by global L2 norm first, exactly as
+                               clip_grad_norm(max_grad_norm) before step(); default 0 */
+    int32_t use_loss_scaler;/* 1: grads arrive multiplied by the loss scale; unscale,
+                               skip on inf/NaN, dynamic scale update. default 0 */
+    float init_scale;       /* 65536 */
+    float growth_factor;    /* 2 */
+    float backoff_factor;   /* 0.5 */
+    int32_t growth_interval;/* 200 clean steps */
+    int32_t device;         /* CUDA device ordinal of every buffer; default 0 */
+} soar_adamw_opts;
+
+/* Step bookkeeping, read back from the device (soar_optim_get_info). */
+typedef struct soar_step_info {
+    uint64_t step;          /* AdamW step count t (adamw.hpp:35); skipped steps excluded */
+    uint64_t skipped;       /* steps skipped for inf/NaN */
+    float grad_norm;        /* pre-clip global norm of the last step (clip_grad_norm's return) */
+    int32_t found_inf;      /* last step saw a non-finite unscaled gradient */
+    float clip_coef;        /* coefficient applied by the last step (1 = none) */
+    float loss_scale;       /* live loss scale (for the next backward) */
+    int32_t growth_tracker; /* clean steps since the last scale change */
+    float lr;               /* learning rate used by the last step */
+} soar_step_info;
+
+/* Reference-default options (adamw.hpp:10-16) and the extension defaults. */
+SOAR_API void soar_adamw_default_opts(soar_adamw_opts* out);
+
+/* Replaces AdamW::AdamW(std::vector<TensorPtr>, AdamWOptions) (adamw.cpp:66-77):
+   allocates the optimizer state (m = v = 0; master = float(param) in the mixed
+   layout) and the tensor-list chunk table on opts->device. */
+SOAR_API int soar_optim_create(const soar_tensor_desc* tensors, int n_tensors,
+                               const soar_adamw_opts* opts, void** out_handle);
+
+/* Same, with every tensor's weight decay taken from opts->weight_decay (the
+   reference constructor's single weight_decay, adamw.hpp:15). */
+SOAR_API int soar_optim_create_uniform(void* const* params, void* const* grads,
+                                       const uint64_t* numel, int n_tensors,
+                                       const soar_adamw_opts* opts, void** out_handle);
+
+SOAR_API int soar_optim_destroy(void* handle);
+
+/* Replaces AdamW::step() (adamw.cpp:119-176) -- and, with max_grad_norm > 0,
+   the clip_grad_norm() call before it (adamw.cpp:87-117) -- as one fused
+   device step: unscale, inf/NaN detect, global norm, clip, AdamW with
+   per-tensor wd on the fp32 master, bf16 write-back, loss-scale update.
+   Enqueued on `stream`; never synchronises the host. */
+SOAR_API int soar_optim_step(void* handle, void* stream);
+
+/* Replaces AdamW::clip_grad_norm(max_norm) (adamw.cpp:87-117): returns the
+   pre-clip global L2 norm in *out_norm and, when norm > max_norm and
+   norm > 1e-6, scales the fp32 grads in place by max_norm/norm. In the mixed
+   layout the bf16 grads are left untouched and the coefficient is applied in
+   fp32 inside the next step(). With the loss scaler on, the norm is that of
+   the unscaled grads. Synchronous (it returns a value, as the reference does). */
+SOAR_API int soar_optim_clip_grad_norm(void* handle, float max_norm, float* out_norm,
+                                       void* stream);
+
+/* Replaces AdamW::zero_grad() (adamw.cpp:79-85): zeroes every gradient. */
+SOAR_API int soar_optim_zero_grad(void* handle, void* stream);
+
+/* Replace AdamW::set_lr / get_lr (adamw.hpp:29-30). Host-side, no device work. */
+SOAR_API int soar_optim_set_lr(void* handle, float lr);
+SOAR_API int soar_optim_get_lr(void* handle, float* out_lr);
+
+/* Step bookkeeping readback (synchronises `stream`). No reference counterpart
+   beyond get_lr; the reference keeps step_count_ private (adamw.hpp:35). */
+SOAR_API int soar_optim_get_info(void* handle, soar_step_info* out, void* stream);
+
+/* Restores step count, skip count, loss scale and growth tracker (resume). */
+SOAR_API int soar_optim_set_counters(void* handle, uint64_t step, uint64_t skipped,
+                                     float loss_scale, int32_t growth_tracker, void* stream);
+
+/* Device address of tensor `index`'s optimizer state array (`kind`:
+   enum soar_state_kind; MASTER is the param itself in the FP32 layout). The
+   reference holds these as m_[idx] / v_[idx] (adamw.hpp:38-39). */
+SOAR_API int soar_optim_state_ptr(void* handle, int index, int kind, void** out_ptr);
+
+/* Synchronous host copies of one tensor's state (checkpointing, tests). */
+SOAR_API int soar_optim_read_state(void* handle, int index, int kind, float* host_dst);
+SOAR_API int soar_optim_write_state(void* handle, int index, int kind, const float* host_src);
+
+/* Device address of the live loss scale (fp32), for scaling the loss on the
+   device without a host round trip. */
+SOAR_API int soar_optim_loss_scale_ptr(void* handle, float** out_ptr);
+
+/* Data-parallel split of soar_optim_step (ZeRO-1, one process per GPU):
+   (1) soar_optim_grad_sumsq writes this rank's sum of squared unscaled grads
+       (fp64) to the device address d_sumsq;
+   (2) the caller gathers the R partials of all ranks into one device array
+       (e.g. an all-gather over NCCL);
+   (3) soar_optim_apply sums the partials in rank order -- so every rank takes
+       the same skip/clip decision from identical bits -- and runs the update.
+   With n_parts = 0 (and d_parts NULL) apply runs without norm/inf
+   information: no clip and no skip. */
+SOAR_API int soar_optim_grad_sumsq(void* handle, double* d_sumsq, void* stream);
+SOAR_API int soar_optim_apply(void* handle, const double* d_parts, int n_parts, void* stream);
+
+/* Replaces CosineAnnealingLR (adamw.hpp:45-57, adamw.cpp:178-202): linear
+   warmup, cosine decay to eta_min, eta_min past the end; each step() sets the
+   bound optimizer's lr (host-side float math, the reference's expressions).
+   The scheduler keeps the optimizer handle, so moving the optimizer between
+   owners cannot leave it bound to a stale object. */
+SOAR_API int soar_cosine_create(void* optim_handle, uint64_t total_steps, float eta_min,
+                                uint64_t warmup_steps, void** out_handle);
+SOAR_API int soar_cosine_step(void* sched_handle);
+SOAR_API int soar_cosine_destroy(void* sched_handle);
+
+/* Message of the calling thread's last failed call ("" if none). */
+SOAR_API const char* soar_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SOAR_OPTIM_H */

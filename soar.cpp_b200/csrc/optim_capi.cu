@@ -1,0 +1,637 @@
+// Host side of the optimizer-step C-ABI (include/soar_optim.h).
+//
+// Owns, per optimizer, one device slab carved DeviceSlab-style (aligned bump
+// offsets over a single cudaMalloc; the reference's DeviceSlabSubAllocator,
+// src/memory/device_slab.cpp:6-38) holding the fp32 master weights, m, v, the
+// chunk table, the per-CTA reduction partials and the step control block.
+// Builds the tensor-list chunk table once at create time, so a step is two
+// kernel launches with no host work beyond filling the launch arguments.
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "../../include/soar_optim.h"
+#include "optim_kernels.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(const std::string& msg) {
+    g_last_error = msg;
+    return SOAR_ERROR;
+}
+
+#define SOAR_CUDA_TRY(expr)                                                              \
+    do {                                                                                 \
+        cudaError_t e_ = (expr);                                                         \
+        if (e_ != cudaSuccess) return fail(std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+// Makes the optimizer's device current for the scope of one call.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = false;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        ok = (prev == dev) || (cudaSetDevice(dev) == cudaSuccess);
+    }
+    ~DeviceGuard() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
+
+constexpr size_t kSlabAlign = 256;
+constexpr uint32_t kBcCap = 1u << 22;  // bias-correction table entries before it must converge
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct TensorRec {
+    void* param;
+    void* grad;
+    uint64_t numel;
+    float wd;
+    uint64_t state_off;  // element offset of this tensor's master/m/v slices
+};
+
+struct Optim {
+    int device = 0;
+    bool mixed = false;
+    soar_adamw_opts opts{};
+    float lr = 1e-3f;
+    float pending_coef = 1.0f;   // from a standalone clip_grad_norm (mixed layout)
+    uint64_t host_calls = 0;     // step() calls issued: an upper bound of the device t
+
+    std::vector<TensorRec> tensors;
+    uint64_t state_elems = 0;
+
+    char* slab = nullptr;
+    float* master = nullptr;     // mixed only
+    float* m = nullptr;
+    float* v = nullptr;
+    soarb::Chunk* chunks = nullptr;
+    int n_chunks = 0;
+    double* partials = nullptr;
+    soarb::Ctl* ctl = nullptr;
+    double* sumsq_scratch = nullptr;
+
+    float2* bc = nullptr;        // separate allocation (it can grow)
+    uint32_t bc_len = 0;
+    bool bc_converged = false;
+
+    int grid_sumsq = 1;
+    int grid_apply = 1;
+    std::vector<soarb::Chunk> host_chunks;
+};
+
+struct Cosine {
+    Optim* opt;
+    float base_lr;
+    float eta_min;
+    uint64_t total_steps;
+    uint64_t warmup_steps;
+    uint64_t current_step = 0;
+};
+
+size_t elem_bytes(const Optim& o) { return o.mixed ? 2 : 4; }
+
+// bc[t] = (1 - beta1^t, sqrt(1 - beta2^t)) with the reference's own host
+// expressions (adamw.cpp:127-129), so the device reads the reference's bits.
+std::vector<float2> bias_table(float beta1, float beta2, uint32_t len, bool* converged) {
+    std::vector<float2> tab(len);
+    tab[0] = make_float2(1.0f, 1.0f);  // t = 0 is never used
+    *converged = false;
+    uint32_t ones_run = 0;
+    for (uint32_t t = 1; t < len; ++t) {
+        const float bias_correction1 = 1.0f - std::pow(beta1, static_cast<float>(t));
+        const float bias_correction2 = 1.0f - std::pow(beta2, static_cast<float>(t));
+        tab[t] = make_float2(bias_correction1, std::sqrt(bias_correction2));
+        ones_run = (bias_correction1 == 1.0f && bias_correction2 == 1.0f) ? ones_run + 1 : 0;
+        // Both corrections are exactly 1 from here on (beta^t only shrinks);
+        // keep 4096 such entries as a margin and stop.
+        if (ones_run == 4096) {
+            tab.resize(t + 1);
+            *converged = true;
+            break;
+        }
+    }
+    return tab;
+}
+
+int upload_bias_table(Optim& o, uint32_t len) {
+    bool conv = false;
+    std::vector<float2> tab = bias_table(o.opts.beta1, o.opts.beta2, len, &conv);
+    float2* d = nullptr;
+    SOAR_CUDA_TRY(cudaMalloc(&d, tab.size() * sizeof(float2)));
+    cudaError_t e = cudaMemcpy(d, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(d);
+        return fail(std::string("bias table upload: ") + cudaGetErrorString(e));
+    }
+    if (o.bc) {
+        cudaDeviceSynchronize();  // earlier steps may still read the old table
+        cudaFree(o.bc);
+    }
+    o.bc = d;
+    o.bc_len = static_cast<uint32_t>(tab.size());
+    o.bc_converged = conv;
+    return SOAR_OK;
+}
+
+// Splits every tensor with a gradient into chunks. A tensor whose param and
+// grad share the same phase modulo the 4-element vector width gets a scalar
+// head (<= 3 elements) and vector chunks after it; its state slices are
+// placed with that same phase. Otherwise its chunks run the scalar path.
+void build_chunks(Optim& o) {
+    const size_t eb = elem_bytes(o);
+    const size_t vbytes = 4 * eb;
+    o.host_chunks.clear();
+    uint64_t cursor = 0;
+    for (size_t ti = 0; ti < o.tensors.size(); ++ti) {
+        TensorRec& t = o.tensors[ti];
+        const uintptr_t pa = reinterpret_cast<uintptr_t>(t.param);
+        const uintptr_t ga = reinterpret_cast<uintptr_t>(t.grad);
+        const uint64_t pphase = (pa % vbytes) / eb;
+        const uint64_t gphase = t.grad ? (ga % vbytes) / eb : pphase;
+        // 256-byte aligned slice start, shifted by the param's element phase.
+        t.state_off = align_up(cursor, 64) + pphase;
+        cursor = t.state_off + t.numel;
+        if (!t.grad || t.numel == 0) continue;
+        const bool vec_ok = (pphase == gphase);
+        const uint64_t head = vec_ok ? (4 - pphase) % 4 : 0;
+        auto add = [&](uint64_t start, uint64_t len, bool vec) {
+            soarb::Chunk c{};
+            c.param = static_cast<char*>(t.param) + start * eb;
+            c.grad = static_cast<const char*>(t.grad) + start * eb;
+            c.n = static_cast<uint32_t>(len);
+            c.wd = t.wd;
+            c.flags = vec ? soarb::kChunkVec : 0u;
+            c.tensor = static_cast<uint32_t>(ti);
+            // master/m/v pointers are filled once the slab exists
+            c.master = reinterpret_cast<float*>(static_cast<uintptr_t>(t.state_off + start));
+            o.host_chunks.push_back(c);
+        };
+        const uint64_t h = std::min<uint64_t>(head, t.numel);
+        if (h) add(0, h, false);
+        for (uint64_t s = h; s < t.numel; s += soarb::kChunkElems)
+            add(s, std::min<uint64_t>(soarb::kChunkElems, t.numel - s), vec_ok);
+    }
+    o.state_elems = align_up(cursor, 64);
+}
+
+int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* opts,
+                void** out) {
+    if (!opts || !out || n < 0 || (n > 0 && !tensors)) return fail("null argument");
+    *out = nullptr;
+    if (opts->layout != SOAR_LAYOUT_FP32 && opts->layout != SOAR_LAYOUT_BF16_MIXED)
+        return fail("unknown layout");
+    if (opts->use_loss_scaler && !(opts->init_scale > 0.0f)) return fail("init_scale must be > 0");
+    if (opts->use_loss_scaler && opts->growth_interval <= 0) return fail("growth_interval must be > 0");
+
+    auto* o = new Optim();
+    o->opts = *opts;
+    o->device = opts->device;
+    o->mixed = opts->layout == SOAR_LAYOUT_BF16_MIXED;
+    o->lr = opts->lr;
+    const size_t eb = elem_bytes(*o);
+    for (int i = 0; i < n; ++i) {
+        const soar_tensor_desc& d = tensors[i];
+        if (d.numel > 0 && !d.param) {
+            delete o;
+            return fail("tensor " + std::to_string(i) + ": null param");
+        }
+        if ((reinterpret_cast<uintptr_t>(d.param) % eb) || (reinterpret_cast<uintptr_t>(d.grad) % eb)) {
+            delete o;
+            return fail("tensor " + std::to_string(i) + ": pointer not aligned to its element size");
+        }
+        o->tensors.push_back({d.param, d.grad, d.numel, d.weight_decay, 0});
+    }
+
+    DeviceGuard g(o->device);
+    if (!g.ok) {
+        delete o;
+        return fail("cannot select device " + std::to_string(opts->device));
+    }
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, o->device) != cudaSuccess ||
+        sms <= 0) {
+        delete o;
+        return fail("cannot query the SM count");
+    }
+    build_chunks(*o);
+    o->n_chunks = static_cast<int>(o->host_chunks.size());
+    const int cap = std::max(1, o->n_chunks);
+    o->grid_sumsq = std::min(sms * soarb::occupancy_grad_sumsq(o->mixed), cap);
+    o->grid_apply = std::min(sms * soarb::occupancy_apply(o->mixed), cap);
+
+    // Slab: [master | m | v | chunks | partials | ctl | clip scratch]
+    const size_t state_bytes = o->state_elems * sizeof(float);
+    size_t off = 0;
+    const size_t off_master = off;
+    if (o->mixed) off = align_up(off + state_bytes, kSlabAlign);
+    const size_t off_m = off;
+    off = align_up(off + state_bytes, kSlabAlign);
+    const size_t off_v = off;
+    off = align_up(off + state_bytes, kSlabAlign);
+    const size_t off_chunks = off;
+    off = align_up(off + o->host_chunks.size() * sizeof(soarb::Chunk), kSlabAlign);
+    const size_t off_partials = off;
+    off = align_up(off + o->grid_sumsq * sizeof(double), kSlabAlign);
+    const size_t off_ctl = off;
+    off = align_up(off + sizeof(soarb::Ctl), kSlabAlign);
+    const size_t off_scratch = off;
+    off = align_up(off + sizeof(double), kSlabAlign);
+
+    cudaError_t e = cudaMalloc(&o->slab, off);
+    if (e != cudaSuccess) {
+        delete o;
+        return fail(std::string("optimizer slab (") + std::to_string(off) + " bytes): " +
+                    cudaGetErrorString(e));
+    }
+    o->master = o->mixed ? reinterpret_cast<float*>(o->slab + off_master) : nullptr;
+    o->m = reinterpret_cast<float*>(o->slab + off_m);
+    o->v = reinterpret_cast<float*>(o->slab + off_v);
+    o->chunks = reinterpret_cast<soarb::Chunk*>(o->slab + off_chunks);
+    o->partials = reinterpret_cast<double*>(o->slab + off_partials);
+    o->ctl = reinterpret_cast<soarb::Ctl*>(o->slab + off_ctl);
+    o->sumsq_scratch = reinterpret_cast<double*>(o->slab + off_scratch);
+
+    for (soarb::Chunk& c : o->host_chunks) {
+        const uint64_t s = static_cast<uint64_t>(reinterpret_cast<uintptr_t>(c.master));
+        c.master = o->mixed ? o->master + s : static_cast<float*>(c.param);
+        c.m = o->m + s;
+        c.v = o->v + s;
+    }
+
+    auto cleanup = [&](const std::string& msg) {
+        cudaFree(o->slab);
+        if (o->bc) cudaFree(o->bc);
+        delete o;
+        return fail(msg);
+    };
+    if ((e = cudaMemcpy(o->chunks, o->host_chunks.data(),
+                        o->host_chunks.size() * sizeof(soarb::Chunk), cudaMemcpyHostToDevice)) !=
+        cudaSuccess)
+        return cleanup(std::string("chunk table upload: ") + cudaGetErrorString(e));
+    if ((e = cudaMemset(o->m, 0, state_bytes)) != cudaSuccess ||
+        (e = cudaMemset(o->v, 0, state_bytes)) != cudaSuccess)
+        return cleanup(std::string("state zero-fill: ") + cudaGetErrorString(e));
+    soarb::Ctl ctl{};
+    ctl.scale = opts->use_loss_scaler ? opts->init_scale : 1.0f;
+    ctl.last_clip_coef = 1.0f;
+    ctl.last_lr = opts->lr;
+    if ((e = cudaMemcpy(o->ctl, &ctl, sizeof ctl, cudaMemcpyHostToDevice)) != cudaSuccess)
+        return cleanup(std::string("control block upload: ") + cudaGetErrorString(e));
+    if (o->mixed) {
+        // master = float(bf16 param): exact
+        if ((e = cudaMemset(o->master, 0, state_bytes)) != cudaSuccess)
+            return cleanup(std::string("master zero-fill: ") + cudaGetErrorString(e));
+        for (const TensorRec& t : o->tensors) {
+            if (!t.numel) continue;
+            if ((e = soarb::launch_bf16_to_f32(static_cast<const uint16_t*>(t.param),
+                                               o->master + t.state_off, t.numel, nullptr)) !=
+                cudaSuccess)
+                return cleanup(std::string("master init: ") + cudaGetErrorString(e));
+        }
+    }
+    {
+        // sized for the first 64K steps, grown on demand until it converges
+        const int rc = upload_bias_table(*o, 1u << 16);
+        if (rc != SOAR_OK) return cleanup(g_last_error);
+    }
+    if ((e = cudaDeviceSynchronize()) != cudaSuccess)
+        return cleanup(std::string("create: ") + cudaGetErrorString(e));
+    *out = o;
+    return SOAR_OK;
+}
+
+int ensure_bias_table(Optim& o) {
+    if (o.bc_converged || o.host_calls + 1 < o.bc_len) return SOAR_OK;
+    const uint64_t want = std::min<uint64_t>(static_cast<uint64_t>(o.bc_len) * 2, kBcCap);
+    if (want <= o.bc_len) return fail("bias-correction table cap reached without converging");
+    return upload_bias_table(o, static_cast<uint32_t>(want));
+}
+
+soarb::ApplyArgs apply_args(const Optim& o, const double* parts, int n_parts) {
+    soarb::ApplyArgs a{};
+    a.lr = o.lr;
+    a.beta1 = o.opts.beta1;
+    a.beta2 = o.opts.beta2;
+    a.eps = o.opts.eps;
+    a.max_norm = o.opts.max_grad_norm;
+    a.pending_coef = o.pending_coef;
+    a.growth = o.opts.growth_factor;
+    a.backoff = o.opts.backoff_factor;
+    a.interval = o.opts.growth_interval;
+    a.use_scaler = o.opts.use_loss_scaler;
+    a.n_parts = n_parts;
+    a.parts = parts;
+    a.bc = o.bc;
+    a.bc_len = o.bc_len;
+    return a;
+}
+
+int apply_impl(Optim& o, const double* parts, int n_parts, cudaStream_t s) {
+    if (n_parts < 0 || (n_parts > 0 && !parts)) return fail("bad partial sums");
+    int rc = ensure_bias_table(o);
+    if (rc != SOAR_OK) return rc;
+    const soarb::ApplyArgs a = apply_args(o, parts, n_parts);
+    SOAR_CUDA_TRY(soarb::launch_apply(o.mixed, o.chunks, o.n_chunks, o.ctl, a, o.grid_apply, s));
+    o.host_calls += 1;
+    o.pending_coef = 1.0f;
+    return SOAR_OK;
+}
+
+int sumsq_impl(Optim& o, double* out, cudaStream_t s) {
+    SOAR_CUDA_TRY(soarb::launch_grad_sumsq(o.mixed, o.chunks, o.n_chunks, o.ctl, o.partials,
+                                           o.grid_sumsq, o.opts.use_loss_scaler, out, s));
+    return SOAR_OK;
+}
+
+Optim* as_optim(void* h) { return static_cast<Optim*>(h); }
+
+}  // namespace
+
+extern "C" {
+
+SOAR_API void soar_adamw_default_opts(soar_adamw_opts* out) {
+    if (!out) return;
+    std::memset(out, 0, sizeof *out);
+    out->lr = 1e-3f;
+    out->beta1 = 0.9f;
+    out->beta2 = 0.999f;
+    out->eps = 1e-8f;
+    out->weight_decay = 1e-2f;
+    out->layout = SOAR_LAYOUT_FP32;
+    out->max_grad_norm = 0.0f;
+    out->use_loss_scaler = 0;
+    out->init_scale = 65536.0f;
+    out->growth_factor = 2.0f;
+    out->backoff_factor = 0.5f;
+    out->growth_interval = 200;
+    out->device = 0;
+}
+
+SOAR_API int soar_optim_create(const soar_tensor_desc* tensors, int n_tensors,
+                               const soar_adamw_opts* opts, void** out_handle) {
+    try {
+        return create_impl(tensors, n_tensors, opts, out_handle);
+    } catch (const std::exception& ex) {
+        return fail(ex.what());
+    } catch (...) {
+        return fail("unknown exception");
+    }
+}
+
+SOAR_API int soar_optim_create_uniform(void* const* params, void* const* grads,
+                                       const uint64_t* numel, int n_tensors,
+                                       const soar_adamw_opts* opts, void** out_handle) {
+    if (!opts || n_tensors < 0 || (n_tensors > 0 && (!params || !numel)))
+        return fail("null argument");
+    try {
+        std::vector<soar_tensor_desc> d(static_cast<size_t>(n_tensors));
+        for (int i = 0; i < n_tensors; ++i)
+            d[i] = {params[i], grads ? grads[i] : nullptr, numel[i], opts->weight_decay};
+        return create_impl(d.data(), n_tensors, opts, out_handle);
+    } catch (...) {
+        return fail("exception in create_uniform");
+    }
+}
+
+SOAR_API int soar_optim_destroy(void* handle) {
+    if (!handle) return fail("null handle");
+    Optim* o = as_optim(handle);
+    {
+        DeviceGuard g(o->device);
+        cudaDeviceSynchronize();
+        cudaFree(o->slab);
+        if (o->bc) cudaFree(o->bc);
+    }
+    delete o;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_optim_step(void* handle, void* stream) {
+    if (!handle) return fail("null handle");
+    Optim& o = *as_optim(handle);
+    DeviceGuard g(o.device);
+    if (!g.ok) return fail("cannot select the optimizer's device");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool need_norm = o.opts.use_loss_scaler || o.opts.max_grad_norm > 0.0f;
+    if (need_norm) {
+        double* d_sumsq = &o.ctl->sumsq;
+        int rc = sumsq_impl(o, d_sumsq, s);
+        if (rc != SOAR_OK) return rc;
+        return apply_impl(o, d_sumsq, 1, s);
+    }
+    return apply_impl(o, nullptr, 0, s);
+}
+
+SOAR_API int soar_optim_grad_sumsq(void* handle, double* d_sumsq, void* stream) {
+    if (!handle || !d_sumsq) return fail("null argument");
+    Optim& o = *as_optim(handle);
+    DeviceGuard g(o.device);
+    return sumsq_impl(o, d_sumsq, static_cast<cudaStream_t>(stream));
+}
+
+SOAR_API int soar_optim_apply(void* handle, const double* d_parts, int n_parts, void* stream) {
+    if (!handle) return fail("null handle");
+    Optim& o = *as_optim(handle);
+    DeviceGuard g(o.device);
+    return apply_impl(o, d_parts, n_parts, static_cast<cudaStream_t>(stream));
+}
+
+SOAR_API int soar_optim_clip_grad_norm(void* handle, float max_norm, float* out_norm,
+                                       void* stream) {
+    if (!handle || !out_norm) return fail("null argument");
+    Optim& o = *as_optim(handle);
+    DeviceGuard g(o.device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int rc = sumsq_impl(o, o.sumsq_scratch, s);
+    if (rc != SOAR_OK) return rc;
+    double total = 0.0;
+    SOAR_CUDA_TRY(cudaMemcpyAsync(&total, o.sumsq_scratch, sizeof total, cudaMemcpyDeviceToHost, s));
+    SOAR_CUDA_TRY(cudaStreamSynchronize(s));
+    // adamw.cpp:101-103
+    const float total_norm = static_cast<float>(std::sqrt(total));
+    if (total_norm > max_norm && total_norm > 1e-6f) {
+        const float clip_coef = max_norm / total_norm;
+        if (o.mixed) {
+            o.pending_coef = clip_coef;
+        } else {
+            SOAR_CUDA_TRY(soarb::launch_scale_grads_f32(o.chunks, o.n_chunks, clip_coef,
+                                                        o.grid_apply, s));
+        }
+    }
+    *out_norm = total_norm;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_optim_zero_grad(void* handle, void* stream) {
+    if (!handle) return fail("null handle");
+    Optim& o = *as_optim(handle);
+    DeviceGuard g(o.device);
+    const size_t eb = elem_bytes(o);
+    // coalesce adjacent gradient buffers into single memsets
+    std::vector<std::pair<char*, size_t>> r;
+    for (const TensorRec& t : o.tensors)
+        if (t.grad && t.numel) r.emplace_back(static_cast<char*>(t.grad), t.numel * eb);
+    std::sort(r.begin(), r.end());
+    size_t i = 0;
+    while (i < r.size()) {
+        char* p = r[i].first;
+        char* end = p + r[i].second;
+        size_t j = i + 1;
+        while (j < r.size() && r[j].first <= end) {
+            end = std::max(end, r[j].first + r[j].second);
+            ++j;
+        }
+        SOAR_CUDA_TRY(cudaMemsetAsync(p, 0, static_cast<size_t>(end - p),
+                                      static_cast<cudaStream_t>(stream)));
+        i = j;
+    }
+    return SOAR_OK;
+}
+
+SOAR_API int soar_optim_set_lr(void* handle, float lr) {
+    if (!handle) return fail("null handle");
+    as_optim(handle)->lr = lr;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_optim_get_lr(void* handle, float* out_lr) {
+    if (!handle || !out_lr) return fail("null argument");
+    *out_lr = as_optim(handle)->lr;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_optim_get_info(void* handle, soar_step_info* out, void* stream) {
+    if (!handle || !out) return fail("null argument");
+    Optim& o = *as_optim(handle);
+    DeviceGuard g(o.device);
+    soarb::Ctl c{};
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    SOAR_CUDA_TRY(cudaMemcpyAsync(&c, o.ctl, sizeof c, cudaMemcpyDeviceToHost, s));
+    SOAR_CUDA_TRY(cudaStreamSynchronize(s));
+    out->step = c.t;
+    out->skipped = c.skipped;
+    out->grad_norm = c.last_norm;
+    out->found_inf = c.last_found_inf;
+    out->clip_coef = c.last_clip_coef;
+    out->loss_scale = c.scale;
+    out->growth_tracker = c.tracker;
+    out->lr = c.last_lr;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_optim_set_counters(void* handle, uint64_t step, uint64_t skipped,
+                                     float loss_scale, int32_t growth_tracker, void* stream) {
+    if (!handle) return fail("null handle");
+    Optim& o = *as_optim(handle);
+    DeviceGuard g(o.device);
+    SOAR_CUDA_TRY(soarb::launch_set_counters(o.ctl, step, skipped, loss_scale, growth_tracker,
+                                             static_cast<cudaStream_t>(stream)));
+    o.host_calls = std::max(o.host_calls, step + skipped);
+    return ensure_bias_table(o);
+}
+
+SOAR_API int soar_optim_state_ptr(void* handle, int index, int kind, void** out_ptr) {
+    if (!handle || !out_ptr) return fail("null argument");
+    Optim& o = *as_optim(handle);
+    if (index < 0 || static_cast<size_t>(index) >= o.tensors.size()) return fail("bad tensor index");
+    const TensorRec& t = o.tensors[index];
+    switch (kind) {
+        case SOAR_STATE_MASTER:
+            *out_ptr = o.mixed ? static_cast<void*>(o.master + t.state_off) : t.param;
+            return SOAR_OK;
+        case SOAR_STATE_M:
+            *out_ptr = o.m + t.state_off;
+            return SOAR_OK;
+        case SOAR_STATE_V:
+            *out_ptr = o.v + t.state_off;
+            return SOAR_OK;
+        default:
+            return fail("bad state kind");
+    }
+}
+
+SOAR_API int soar_optim_read_state(void* handle, int index, int kind, float* host_dst) {
+    void* p = nullptr;
+    if (!host_dst) return fail("null argument");
+    int rc = soar_optim_state_ptr(handle, index, kind, &p);
+    if (rc != SOAR_OK) return rc;
+    Optim& o = *as_optim(handle);
+    DeviceGuard g(o.device);
+    SOAR_CUDA_TRY(cudaDeviceSynchronize());
+    SOAR_CUDA_TRY(cudaMemcpy(host_dst, p, o.tensors[index].numel * sizeof(float),
+                             cudaMemcpyDeviceToHost));
+    return SOAR_OK;
+}
+
+SOAR_API int soar_optim_write_state(void* handle, int index, int kind, const float* host_src) {
+    void* p = nullptr;
+    if (!host_src) return fail("null argument");
+    int rc = soar_optim_state_ptr(handle, index, kind, &p);
+    if (rc != SOAR_OK) return rc;
+    Optim& o = *as_optim(handle);
+    DeviceGuard g(o.device);
+    SOAR_CUDA_TRY(cudaDeviceSynchronize());
+    SOAR_CUDA_TRY(cudaMemcpy(p, host_src, o.tensors[index].numel * sizeof(float),
+                             cudaMemcpyHostToDevice));
+    return SOAR_OK;
+}
+
+SOAR_API int soar_optim_loss_scale_ptr(void* handle, float** out_ptr) {
+    if (!handle || !out_ptr) return fail("null argument");
+    *out_ptr = &as_optim(handle)->ctl->scale;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_cosine_create(void* optim_handle, uint64_t total_steps, float eta_min,
+                                uint64_t warmup_steps, void** out_handle) {
+    if (!optim_handle || !out_handle) return fail("null argument");
+    Optim* o = as_optim(optim_handle);
+    // adamw.cpp:178-180: base lr is the optimizer's lr at construction
+    *out_handle = new (std::nothrow) Cosine{o, o->lr, eta_min, total_steps, warmup_steps, 0};
+    return *out_handle ? SOAR_OK : fail("out of host memory");
+}
+
+SOAR_API int soar_cosine_step(void* sched_handle) {
+    if (!sched_handle) return fail("null handle");
+    Cosine& c = *static_cast<Cosine*>(sched_handle);
+    // adamw.cpp:182-201, same types and expressions
+    c.current_step++;
+    if (c.current_step <= c.warmup_steps && c.warmup_steps > 0) {
+        const float lr = c.base_lr * static_cast<float>(c.current_step) /
+                         static_cast<float>(c.warmup_steps);
+        c.opt->lr = lr;
+        return SOAR_OK;
+    }
+    const uint64_t adjusted_step = c.current_step - c.warmup_steps;
+    const uint64_t adjusted_total = c.total_steps - c.warmup_steps;
+    if (adjusted_step > adjusted_total) {
+        c.opt->lr = c.eta_min;
+        return SOAR_OK;
+    }
+    constexpr float pi = 3.14159265358979323846f;
+    const float progress = static_cast<float>(adjusted_step) / static_cast<float>(adjusted_total);
+    const float lr = c.eta_min + 0.5f * (c.base_lr - c.eta_min) * (1.0f + std::cos(progress * pi));
+    c.opt->lr = lr;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_cosine_destroy(void* sched_handle) {
+    if (!sched_handle) return fail("null handle");
+    delete static_cast<Cosine*>(sched_handle);
+    return SOAR_OK;
+}
+
+SOAR_API const char* soar_last_error(void) { return g_last_error.c_str(); }
+
+}  // extern "C"

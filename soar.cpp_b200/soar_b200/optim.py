@@ -1,0 +1,342 @@
+"""Python mirror of the reference's optimizer API over the sm_100a C-ABI.
+
+The reference binds its C-ABI with ctypes (soar/__init__.py:48-95); this
+module binds include/soar_optim.h the same way and mirrors
+soar::optim::AdamW / AdamWOptions / CosineAnnealingLR
+(include/soar/optim/adamw.hpp:10-57): same class names, the same methods
+(step, zero_grad, clip_grad_norm, set_lr, get_lr) with the same argument
+meaning, and failures raised as exceptions (the reference's C++ layer throws;
+its C-ABI maps any failure to -1, which this wrapper turns back into an
+exception carrying soar_last_error()).
+
+Parameters and gradients are CUDA tensors (anything with ``data_ptr()``,
+``numel()`` and, for params, ``.grad``); the optimizer state lives in the
+library's own device slab. There is no CPU fallback: without the compiled
+library every call fails.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, field
+from pathlib import Path
+
+from . import _build
+
+LAYOUT_FP32 = 0
+LAYOUT_BF16_MIXED = 1
+STATE_MASTER, STATE_M, STATE_V = 0, 1, 2
+
+
+class SoarError(RuntimeError):
+    pass
+
+
+class TensorDesc(C.Structure):
+    _fields_ = [("param", C.c_void_p), ("grad", C.c_void_p), ("numel", C.c_uint64),
+                ("weight_decay", C.c_float)]
+
+
+class AdamWOpts(C.Structure):
+    _fields_ = [("lr", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float),
+                ("eps", C.c_float), ("weight_decay", C.c_float), ("layout", C.c_int32),
+                ("max_grad_norm", C.c_float), ("use_loss_scaler", C.c_int32),
+                ("init_scale", C.c_float), ("growth_factor", C.c_float),
+                ("backoff_factor", C.c_float), ("growth_interval", C.c_int32),
+                ("device", C.c_int32)]
+
+
+class StepInfo(C.Structure):
+    _fields_ = [("step", C.c_uint64), ("skipped", C.c_uint64), ("grad_norm", C.c_float),
+                ("found_inf", C.c_int32), ("clip_coef", C.c_float), ("loss_scale", C.c_float),
+                ("growth_tracker", C.c_int32), ("lr", C.c_float)]
+
+    def as_dict(self) -> dict:
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
+_lib: C.CDLL | None = None
+
+# name -> (restype, argtypes); every symbol include/soar_optim.h declares
+SIGNATURES: dict[str, tuple] = {
+    "soar_adamw_default_opts": (None, [C.POINTER(AdamWOpts)]),
+    "soar_optim_create": (C.c_int, [C.POINTER(TensorDesc), C.c_int, C.POINTER(AdamWOpts),
+                                    C.POINTER(C.c_void_p)]),
+    "soar_optim_create_uniform": (C.c_int, [C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                                            C.POINTER(C.c_uint64), C.c_int,
+                                            C.POINTER(AdamWOpts), C.POINTER(C.c_void_p)]),
+    "soar_optim_destroy": (C.c_int, [C.c_void_p]),
+    "soar_optim_step": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "soar_optim_clip_grad_norm": (C.c_int, [C.c_void_p, C.c_float, C.POINTER(C.c_float),
+                                            C.c_void_p]),
+    "soar_optim_zero_grad": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "soar_optim_set_lr": (C.c_int, [C.c_void_p, C.c_float]),
+    "soar_optim_get_lr": (C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),
+    "soar_optim_get_info": (C.c_int, [C.c_void_p, C.POINTER(StepInfo), C.c_void_p]),
+    "soar_optim_set_counters": (C.c_int, [C.c_void_p, C.c_uint64, C.c_uint64, C.c_float,
+                                          C.c_int32, C.c_void_p]),
+    "soar_optim_state_ptr": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
+    "soar_optim_read_state": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "soar_optim_write_state": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "soar_optim_loss_scale_ptr": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "soar_optim_grad_sumsq": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
+    "soar_optim_apply": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
+    "soar_cosine_create": (C.c_int, [C.c_void_p, C.c_uint64, C.c_float, C.c_uint64,
+                                     C.POINTER(C.c_void_p)]),
+    "soar_cosine_step": (C.c_int, [C.c_void_p]),
+    "soar_cosine_destroy": (C.c_int, [C.c_void_p]),
+    "soar_last_error": (C.c_char_p, []),
+}
+
+
+def library_path() -> Path:
+    return _build.LIB
+
+
+def lib() -> C.CDLL:
+    """The loaded C-ABI library (built on first use if the .so is absent or stale)."""
+    global _lib
+    if _lib is None:
+        path = _build.build()
+        handle = C.CDLL(str(path))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = lib().soar_last_error().decode(errors="replace")
+        raise SoarError(f"{what} failed: {msg}")
+
+
+def _stream_handle(stream) -> int | None:
+    """cudaStream_t of `stream` (torch.cuda.Stream, int, None -> torch's current)."""
+    if stream is None:
+        try:
+            import torch
+            if torch.cuda.is_available() and torch.cuda.is_initialized():
+                return torch.cuda.current_stream().cuda_stream
+        except Exception:  # pragma: no cover - torch absent
+            pass
+        return None
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+class _DeviceArray:
+    """__cuda_array_interface__ view of library-owned device memory."""
+
+    def __init__(self, ptr: int, n: int, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+@dataclass
+class AdamWOptions:
+    """include/soar/optim/adamw.hpp:10-16, same defaults."""
+
+    lr: float = 1e-3
+    beta1: float = 0.9
+    beta2: float = 0.999
+    eps: float = 1e-8
+    weight_decay: float = 1e-2
+
+
+@dataclass
+class LossScalerOptions:
+    """Dynamic loss scaler (no reference counterpart)."""
+
+    init_scale: float = 65536.0
+    growth_factor: float = 2.0
+    backoff_factor: float = 0.5
+    growth_interval: int = 200
+
+
+@dataclass
+class ParamGroup:
+    """A list of params sharing one weight decay (the per-group wd mask)."""
+
+    params: list
+    weight_decay: float | None = None
+    extra: dict = field(default_factory=dict)
+
+
+class AdamW:
+    """soar::optim::AdamW on the GPU.
+
+    ``params`` is a list of CUDA tensors with ``.grad`` (or ParamGroup objects
+    giving their own weight decay). ``layout`` is "fp32" (the reference's
+    layout) or "bf16_mixed" (bf16 params/grads, fp32 master/m/v). With
+    ``max_grad_norm`` > 0, step() clips first exactly as clip_grad_norm() would.
+    ``grads`` optionally gives the gradient buffers explicitly (else ``p.grad``).
+    """
+
+    def __init__(self, params, options: AdamWOptions | None = None, *, layout: str = "fp32",
+                 max_grad_norm: float = 0.0, loss_scaler: LossScalerOptions | None = None,
+                 device: int | None = None, grads=None):
+        options = options or AdamWOptions()
+        tensors, wds = [], []
+        for p in params:
+            if isinstance(p, ParamGroup):
+                wd = options.weight_decay if p.weight_decay is None else p.weight_decay
+                for q in p.params:
+                    tensors.append(q)
+                    wds.append(wd)
+            else:
+                tensors.append(p)
+                wds.append(options.weight_decay)
+        self.params = tensors
+        # gradients: explicit list (same order as the flattened params) or .grad
+        self.grads = list(grads) if grads is not None else [getattr(p, "grad", None)
+                                                             for p in tensors]
+        if len(self.grads) != len(tensors):
+            raise ValueError("one gradient (or None) per parameter")
+        self.layout = {"fp32": LAYOUT_FP32, "bf16_mixed": LAYOUT_BF16_MIXED}[layout]
+        o = AdamWOpts()
+        lib().soar_adamw_default_opts(C.byref(o))
+        o.lr, o.beta1, o.beta2, o.eps = options.lr, options.beta1, options.beta2, options.eps
+        o.weight_decay = options.weight_decay
+        o.layout = self.layout
+        o.max_grad_norm = max_grad_norm
+        if loss_scaler is not None:
+            o.use_loss_scaler = 1
+            o.init_scale = loss_scaler.init_scale
+            o.growth_factor = loss_scaler.growth_factor
+            o.backoff_factor = loss_scaler.backoff_factor
+            o.growth_interval = loss_scaler.growth_interval
+        if device is None:
+            dev = getattr(tensors[0], "device", None) if tensors else None
+            device = dev.index if dev is not None and dev.index is not None else 0
+        o.device = device
+        self.device = device
+        self.opts = o
+        n = len(tensors)
+        descs = (TensorDesc * max(n, 1))()
+        for i, (p, g, wd) in enumerate(zip(tensors, self.grads, wds)):
+            descs[i].param = p.data_ptr()
+            descs[i].grad = g.data_ptr() if g is not None else None
+            descs[i].numel = p.numel()
+            descs[i].weight_decay = wd
+        self.numel = [p.numel() for p in tensors]
+        self.weight_decays = wds
+        h = C.c_void_p()
+        _check(lib().soar_optim_create(descs, n, C.byref(o), C.byref(h)), "soar_optim_create")
+        self.handle = h
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().soar_optim_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- the reference's methods (adamw.hpp:25-30) --------------------------
+    def step(self, stream=None) -> None:
+        _check(lib().soar_optim_step(self.handle, _stream_handle(stream)), "soar_optim_step")
+
+    def zero_grad(self, stream=None) -> None:
+        _check(lib().soar_optim_zero_grad(self.handle, _stream_handle(stream)),
+               "soar_optim_zero_grad")
+
+    def clip_grad_norm(self, max_norm: float, stream=None) -> float:
+        out = C.c_float()
+        _check(lib().soar_optim_clip_grad_norm(self.handle, max_norm, C.byref(out),
+                                               _stream_handle(stream)),
+               "soar_optim_clip_grad_norm")
+        return out.value
+
+    def set_lr(self, lr: float) -> None:
+        _check(lib().soar_optim_set_lr(self.handle, lr), "soar_optim_set_lr")
+
+    def get_lr(self) -> float:
+        out = C.c_float()
+        _check(lib().soar_optim_get_lr(self.handle, C.byref(out)), "soar_optim_get_lr")
+        return out.value
+
+    # -- extensions ---------------------------------------------------------
+    def info(self, stream=None) -> StepInfo:
+        out = StepInfo()
+        _check(lib().soar_optim_get_info(self.handle, C.byref(out), _stream_handle(stream)),
+               "soar_optim_get_info")
+        return out
+
+    def set_counters(self, step: int, skipped: int, loss_scale: float, growth_tracker: int,
+                     stream=None) -> None:
+        _check(lib().soar_optim_set_counters(self.handle, step, skipped, loss_scale,
+                                             growth_tracker, _stream_handle(stream)),
+               "soar_optim_set_counters")
+
+    def state_ptr(self, index: int, kind: int) -> int:
+        out = C.c_void_p()
+        _check(lib().soar_optim_state_ptr(self.handle, index, kind, C.byref(out)),
+               "soar_optim_state_ptr")
+        return out.value
+
+    def state(self, index: int, kind: int):
+        """Zero-copy torch view of tensor `index`'s master / m / v."""
+        import torch
+        arr = _DeviceArray(self.state_ptr(index, kind), self.numel[index])
+        return torch.as_tensor(arr, device=f"cuda:{self.device}")
+
+    def read_state(self, index: int, kind: int):
+        import numpy as np
+        out = np.empty(self.numel[index], np.float32)
+        _check(lib().soar_optim_read_state(self.handle, index, kind, out.ctypes.data),
+               "soar_optim_read_state")
+        return out
+
+    def write_state(self, index: int, kind: int, values) -> None:
+        import numpy as np
+        v = np.ascontiguousarray(values, dtype=np.float32)
+        if v.size != self.numel[index]:
+            raise ValueError("size mismatch")
+        _check(lib().soar_optim_write_state(self.handle, index, kind, v.ctypes.data),
+               "soar_optim_write_state")
+
+    def loss_scale_ptr(self) -> int:
+        out = C.c_void_p()
+        _check(lib().soar_optim_loss_scale_ptr(self.handle, C.byref(out)),
+               "soar_optim_loss_scale_ptr")
+        return out.value
+
+    def grad_sumsq(self, out_ptr: int, stream=None) -> None:
+        _check(lib().soar_optim_grad_sumsq(self.handle, out_ptr, _stream_handle(stream)),
+               "soar_optim_grad_sumsq")
+
+    def apply(self, parts_ptr: int | None, n_parts: int, stream=None) -> None:
+        _check(lib().soar_optim_apply(self.handle, parts_ptr, n_parts, _stream_handle(stream)),
+               "soar_optim_apply")
+
+
+class CosineAnnealingLR:
+    """soar::optim::CosineAnnealingLR (adamw.hpp:45-57), bound to an AdamW."""
+
+    def __init__(self, optimizer: AdamW, total_steps: int, eta_min: float = 1e-6,
+                 warmup_steps: int = 0):
+        self.optimizer = optimizer
+        h = C.c_void_p()
+        _check(lib().soar_cosine_create(optimizer.handle, total_steps, eta_min, warmup_steps,
+                                        C.byref(h)), "soar_cosine_create")
+        self.handle = h
+
+    def step(self) -> None:
+        _check(lib().soar_cosine_step(self.handle), "soar_cosine_step")
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().soar_cosine_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
