@@ -185,6 +185,27 @@ SOAR_API int soar_cosine_create(void* optim_handle, uint64_t total_steps, float 
 SOAR_API int soar_cosine_step(void* sched_handle);
 SOAR_API int soar_cosine_destroy(void* sched_handle);
 
+/* Allocation-free gradient sum of squares. No counterpart in the reference.
+   For callers that cannot call cudaMalloc: a host runtime that reserves all of
+   a GPU's memory up front in its own pool (an extra cudaMalloc fails or escapes
+   the pool's accounting), or a latency-sensitive loop where cudaMalloc's
+   implicit device-wide synchronisation would stall work in flight. Computes
+   the same quantity as soar_optim_grad_sumsq -- sum over the tensors of
+   (double)(g * inv_scale)^2, fp32 (FP32 layout) or bf16 (BF16_MIXED) grads --
+   into the caller's device fp64 *d_sumsq, without an optimizer handle and
+   without allocating: its scratch (per-CTA partials and a ticket, ~8 KB) is a
+   static device array that every GPU loading the library holds until exit.
+   At most SOAR_NOALLOC_MAX_TENSORS tensors per call (more is rejected with an
+   error); element counts are unlimited. Runs on the current device. The first
+   call on a device also sets up that device (looks up the array's device
+   address); make that first call before any stream capture. All calls share
+   the array: calls whose kernels overlap on the GPU race and give wrong sums,
+   so order them on one stream. */
+#define SOAR_NOALLOC_MAX_TENSORS 64
+SOAR_API int soar_grad_sumsq_noalloc(const void* const* grads, const uint64_t* numel,
+                                     int n_tensors, int layout, float inv_scale,
+                                     double* d_sumsq, void* stream);
+
 /* Message of the calling thread's last failed call ("" if none). */
 SOAR_API const char* soar_last_error(void);
 

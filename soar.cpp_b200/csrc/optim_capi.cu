@@ -358,6 +358,11 @@ Optim* as_optim(void* h) { return static_cast<Optim*>(h); }
 
 }  // namespace
 
+namespace soarb {
+// Lets other translation units of the library report through soar_last_error().
+void record_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace soarb
+
 extern "C" {
 
 SOAR_API void soar_adamw_default_opts(soar_adamw_opts* out) {

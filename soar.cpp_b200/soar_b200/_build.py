@@ -14,7 +14,7 @@ LIBDIR = ROOT / "lib"
 LIB = LIBDIR / "libsoar_optim.so"
 INCLUDE = ROOT.parent / "include"
 
-SOURCES = ["optim_kernels.cu", "optim_capi.cu"]
+SOURCES = ["optim_kernels.cu", "optim_capi.cu", "noalloc_sumsq.cu"]
 HEADERS = ["optim_kernels.cuh"]
 
 NVCC_FLAGS = [

@@ -84,6 +84,9 @@ SIGNATURES: dict[str, tuple] = {
                                      C.POINTER(C.c_void_p)]),
     "soar_cosine_step": (C.c_int, [C.c_void_p]),
     "soar_cosine_destroy": (C.c_int, [C.c_void_p]),
+    "soar_grad_sumsq_noalloc": (C.c_int, [C.POINTER(C.c_void_p), C.POINTER(C.c_uint64),
+                                          C.c_int, C.c_int, C.c_float, C.c_void_p,
+                                          C.c_void_p]),
     "soar_last_error": (C.c_char_p, []),
 }
 
