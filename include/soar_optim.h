@@ -100,6 +100,9 @@ typedef struct soar_step_info {
     float loss_scale;       /* live loss scale (for the next backward) */
     int32_t growth_tracker; /* clean steps since the last scale change */
     float lr;               /* learning rate used by the last step */
+    int32_t error;          /* nonzero: a device-side pipeline wait timed out in some
+                               step; that step is incomplete and the state must not be
+                               trusted (cleared by soar_optim_set_counters) */
 } soar_step_info;
 
 /* Reference-default options (adamw.hpp:10-16) and the extension defaults. */

@@ -1,28 +1,38 @@
 // Optimizer-step kernels for B200 (sm_100a).
 //
 // The step is HBM-bound streaming work (~15 flop per 28 bytes), so it runs on
-// the SIMT pipes with vector loads, not on tensor cores. Two kernels over one
-// tensor-list chunk table (Chunk, optim_kernels.cuh):
+// the SIMT pipes fed by the Tensor Memory Accelerator, not on tensor cores.
+// Two kernels over one tensor-list chunk table (Chunk, optim_kernels.cuh):
 //
-//   k_grad_sumsq  reads every gradient once (2 B bf16 / 4 B fp32 per element),
-//                 unscales it by the live loss scale and accumulates the fp64
-//                 sum of squares: per thread, warp shuffle, block, then a
-//                 single-pass grid reduction (each CTA writes its partial, the
-//                 last CTA to take a ticket folds them in fixed order).
-//                 Non-finite gradients make the sum non-finite, so the same
-//                 number carries the inf/NaN verdict.
+//   k_grad_sumsq  reads every gradient once (2 B bf16 / 4 B fp32 per element,
+//                 16-byte loads), unscales it by the live loss scale and
+//                 accumulates the fp64 sum of squares: per thread, warp
+//                 shuffle, block, then a single-pass grid reduction (each CTA
+//                 writes its partial, the last CTA to take a ticket folds them
+//                 in fixed order). Non-finite gradients make the sum
+//                 non-finite, so the same number carries the inf/NaN verdict.
 //   k_apply       derives skip / clip coefficient / bias corrections from the
-//                 partial sums, then streams the update: unscale, clip,
-//                 decoupled weight decay, AdamW moments, fp32 master update,
-//                 bf16 write-back. It walks the chunks in the reverse order of
+//                 partial sums, then streams the update through a shared-memory
+//                 pipeline: one producer thread issues 1D bulk async copies
+//                 (cp.async.bulk, completion on an mbarrier) of 1024-element
+//                 tiles of grad/master/m/v into a 6-stage ring; 12 consumer
+//                 warps unscale, clip, apply decoupled weight decay and the
+//                 AdamW moments, write master/m/v and the bf16 params back into
+//                 the stage, and one of them bulk-stores the stage to HBM. The
+//                 loads never wait on registers, so many tiles are in flight
+//                 per SM. Chunks are walked in the reverse order of
 //                 k_grad_sumsq so the gradients read last there are still in
-//                 L2 when it starts. The last CTA to finish commits the step
-//                 counters and the loss-scaler update.
+//                 L2. The last CTA to finish commits the step counters and the
+//                 loss-scaler update.
 //
 // Numerics follow the reference's AdamW::step / clip_grad_norm
 // (src/optim/adamw.cpp:87-176) operation for operation with explicitly
 // rounded intrinsics (no contraction, IEEE sqrt and division), so the fp32
 // update reproduces the reference's bits.
+//
+// Every wait on an mbarrier is bounded (1 s of %globaltimer); on timeout the
+// kernel records Ctl::error, stops issuing, waits (bounded) for its own copies
+// in flight and returns.
 #include "optim_kernels.cuh"
 
 #include <cuda_bf16.h>
@@ -47,6 +57,78 @@ __device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo, float hi) {
 
 __device__ __forceinline__ uint16_t f32_to_bf16_rn(float x) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
+// -------------------------------------------------- mbarrier / bulk copies --
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
+
+// Bounded wait for the phase of `bar` with the given parity to complete.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* s_err) {
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try(bar, parity)) return true;
+        if ((i & 1023u) == 0) {
+            if (global_timer_ns() - t0 > kWaitLimitNs) {
+                atomicOr(s_err, 1);
+                return false;
+            }
+            if (*reinterpret_cast<volatile int*>(s_err)) return false;  // another thread gave up
+        }
+    }
+}
+// global -> shared, completes `bytes` of transaction on `bar`
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+// shared -> global, tracked by the issuing thread's bulk groups
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() {
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Named barrier 1 over the kThreadsN consumer threads only.
+template <int kThreadsN>
+__device__ __forceinline__ void consumers_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kThreadsN) : "memory");
 }
 
 // -------------------------------------------------------------- reductions --
@@ -82,6 +164,26 @@ __device__ __forceinline__ double sq_acc(double acc, float g) {
     return fma(d, d, acc);
 }
 
+__device__ __forceinline__ double sq_acc_bf16x8(double acc, const uint4& q, float inv) {
+    acc = sq_acc(acc, __fmul_rn(bf16_lo(q.x), inv));
+    acc = sq_acc(acc, __fmul_rn(bf16_hi(q.x), inv));
+    acc = sq_acc(acc, __fmul_rn(bf16_lo(q.y), inv));
+    acc = sq_acc(acc, __fmul_rn(bf16_hi(q.y), inv));
+    acc = sq_acc(acc, __fmul_rn(bf16_lo(q.z), inv));
+    acc = sq_acc(acc, __fmul_rn(bf16_hi(q.z), inv));
+    acc = sq_acc(acc, __fmul_rn(bf16_lo(q.w), inv));
+    acc = sq_acc(acc, __fmul_rn(bf16_hi(q.w), inv));
+    return acc;
+}
+
+__device__ __forceinline__ double sq_acc_f32x4(double acc, const float4& q, float inv) {
+    acc = sq_acc(acc, __fmul_rn(q.x, inv));
+    acc = sq_acc(acc, __fmul_rn(q.y, inv));
+    acc = sq_acc(acc, __fmul_rn(q.z, inv));
+    acc = sq_acc(acc, __fmul_rn(q.w, inv));
+    return acc;
+}
+
 template <bool kBf16>
 __global__ void __launch_bounds__(kThreads)
 k_grad_sumsq(const Chunk* __restrict__ chunks, int n_chunks, Ctl* __restrict__ ctl,
@@ -96,52 +198,26 @@ k_grad_sumsq(const Chunk* __restrict__ chunks, int n_chunks, Ctl* __restrict__ c
         const void* gp = ch->grad;
         uint32_t scalar_from = 0;
         if (ch->flags & kChunkVec) {
-            const uint32_t nv = n >> 2;
-            scalar_from = nv << 2;
-            if constexpr (kBf16) {
-                const uint2* g4 = static_cast<const uint2*>(gp);
-                uint32_t i = threadIdx.x;
-                for (; i + 3 * kThreads < nv; i += 4 * kThreads) {
-                    uint2 q[4];
+            // 16-byte vectors: 8 bf16 or 4 fp32
+            constexpr uint32_t kPer = kBf16 ? 8u : 4u;
+            const uint32_t nv = n / kPer;
+            scalar_from = nv * kPer;
+            const uint4* g4 = static_cast<const uint4*>(gp);
+            uint32_t i = threadIdx.x;
+            for (; i + 3 * kThreads < nv; i += 4 * kThreads) {
+                uint4 q[4];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) q[u] = __ldg(g4 + i + u * kThreads);
+                for (int u = 0; u < 4; ++u) q[u] = __ldg(g4 + i + u * kThreads);
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        acc = sq_acc(acc, __fmul_rn(bf16_lo(q[u].x), inv));
-                        acc = sq_acc(acc, __fmul_rn(bf16_hi(q[u].x), inv));
-                        acc = sq_acc(acc, __fmul_rn(bf16_lo(q[u].y), inv));
-                        acc = sq_acc(acc, __fmul_rn(bf16_hi(q[u].y), inv));
-                    }
+                for (int u = 0; u < 4; ++u) {
+                    if constexpr (kBf16) acc = sq_acc_bf16x8(acc, q[u], inv);
+                    else acc = sq_acc_f32x4(acc, *reinterpret_cast<const float4*>(&q[u]), inv);
                 }
-                for (; i < nv; i += kThreads) {
-                    const uint2 q = __ldg(g4 + i);
-                    acc = sq_acc(acc, __fmul_rn(bf16_lo(q.x), inv));
-                    acc = sq_acc(acc, __fmul_rn(bf16_hi(q.x), inv));
-                    acc = sq_acc(acc, __fmul_rn(bf16_lo(q.y), inv));
-                    acc = sq_acc(acc, __fmul_rn(bf16_hi(q.y), inv));
-                }
-            } else {
-                const float4* g4 = static_cast<const float4*>(gp);
-                uint32_t i = threadIdx.x;
-                for (; i + 3 * kThreads < nv; i += 4 * kThreads) {
-                    float4 q[4];
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) q[u] = __ldg(g4 + i + u * kThreads);
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        acc = sq_acc(acc, __fmul_rn(q[u].x, inv));
-                        acc = sq_acc(acc, __fmul_rn(q[u].y, inv));
-                        acc = sq_acc(acc, __fmul_rn(q[u].z, inv));
-                        acc = sq_acc(acc, __fmul_rn(q[u].w, inv));
-                    }
-                }
-                for (; i < nv; i += kThreads) {
-                    const float4 q = __ldg(g4 + i);
-                    acc = sq_acc(acc, __fmul_rn(q.x, inv));
-                    acc = sq_acc(acc, __fmul_rn(q.y, inv));
-                    acc = sq_acc(acc, __fmul_rn(q.z, inv));
-                    acc = sq_acc(acc, __fmul_rn(q.w, inv));
-                }
+            }
+            for (; i < nv; i += kThreads) {
+                const uint4 q = __ldg(g4 + i);
+                if constexpr (kBf16) acc = sq_acc_bf16x8(acc, q, inv);
+                else acc = sq_acc_f32x4(acc, *reinterpret_cast<const float4*>(&q), inv);
             }
         }
         for (uint32_t i = scalar_from + threadIdx.x; i < n; i += kThreads) {
@@ -173,87 +249,42 @@ k_grad_sumsq(const Chunk* __restrict__ chunks, int n_chunks, Ctl* __restrict__ c
 
 // ------------------------------------------------------------------ K2 -------
 
-struct Coeffs {
+// Per-step values derived on the device from the control block. The
+// host-known coefficients stay in the launch arguments (kernel parameter
+// space), which keeps them out of the register file of the streaming loop.
+struct StepCoeffs {
     float inv;        // 1 / loss scale
     float coef;       // clip coefficient (1: no clip)
-    float beta1, omb1, beta2, omb2, eps;
     float step_size;  // lr / bias_correction1
     float sqrt_bc2;
-    float lr;
 };
 
 // One element of AdamW::step (adamw.cpp:151-166) on an unscaled, clipped grad.
 __device__ __forceinline__ void adamw_elem(float& th, float& m, float& v, float g,
-                                           const Coeffs& k, float lr_wd, bool has_wd) {
+                                           const ApplyArgs& a, const StepCoeffs& k, float lr_wd,
+                                           bool has_wd) {
     if (has_wd) th = __fsub_rn(th, __fmul_rn(lr_wd, th));
-    m = __fadd_rn(__fmul_rn(k.beta1, m), __fmul_rn(k.omb1, g));
-    v = __fadd_rn(__fmul_rn(k.beta2, v), __fmul_rn(__fmul_rn(k.omb2, g), g));
-    const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(v), k.sqrt_bc2), k.eps);
+    m = __fadd_rn(__fmul_rn(a.beta1, m), __fmul_rn(a.omb1, g));
+    v = __fadd_rn(__fmul_rn(a.beta2, v), __fmul_rn(__fmul_rn(a.omb2, g), g));
+    const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(v), k.sqrt_bc2), a.eps);
     th = __fsub_rn(th, __fmul_rn(k.step_size, __fdiv_rn(m, denom)));
 }
 
 // Unscale (exact for power-of-two scales) then clip (adamw.cpp:108-110).
-__device__ __forceinline__ float prep_grad(float graw, const Coeffs& k) {
+__device__ __forceinline__ float prep_grad(float graw, const StepCoeffs& k) {
     return __fmul_rn(__fmul_rn(graw, k.inv), k.coef);
 }
 
-constexpr int kApplyUnroll = 2;
-
+// Elements [from, to) of a chunk, straight from global memory.
 template <bool kMixed>
-__device__ __forceinline__ void apply_chunk(const Chunk& ch, const Coeffs& k) {
-    const uint32_t n = ch.n;
-    const float lr_wd = __fmul_rn(k.lr, ch.wd);
-    const bool has_wd = ch.wd != 0.0f;
-    uint32_t scalar_from = 0;
-    if (ch.flags & kChunkVec) {
-        const uint32_t nv = n >> 2;
-        scalar_from = nv << 2;
-        float4* ms4 = reinterpret_cast<float4*>(ch.master);
-        float4* m4 = reinterpret_cast<float4*>(ch.m);
-        float4* v4 = reinterpret_cast<float4*>(ch.v);
-        for (uint32_t base = threadIdx.x; base < nv; base += kApplyUnroll * kThreads) {
-            float4 th[kApplyUnroll], mm[kApplyUnroll], vv[kApplyUnroll], gg[kApplyUnroll];
-#pragma unroll
-            for (int u = 0; u < kApplyUnroll; ++u) {
-                const uint32_t i = base + u * kThreads;
-                if (i < nv) {
-                    if constexpr (kMixed) {
-                        const uint2 q = __ldcs(static_cast<const uint2*>(ch.grad) + i);
-                        gg[u] = make_float4(bf16_lo(q.x), bf16_hi(q.x), bf16_lo(q.y), bf16_hi(q.y));
-                    } else {
-                        gg[u] = __ldcs(static_cast<const float4*>(ch.grad) + i);
-                    }
-                    th[u] = __ldcs(ms4 + i);
-                    mm[u] = __ldcs(m4 + i);
-                    vv[u] = __ldcs(v4 + i);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < kApplyUnroll; ++u) {
-                const uint32_t i = base + u * kThreads;
-                if (i < nv) {
-                    adamw_elem(th[u].x, mm[u].x, vv[u].x, prep_grad(gg[u].x, k), k, lr_wd, has_wd);
-                    adamw_elem(th[u].y, mm[u].y, vv[u].y, prep_grad(gg[u].y, k), k, lr_wd, has_wd);
-                    adamw_elem(th[u].z, mm[u].z, vv[u].z, prep_grad(gg[u].z, k), k, lr_wd, has_wd);
-                    adamw_elem(th[u].w, mm[u].w, vv[u].w, prep_grad(gg[u].w, k), k, lr_wd, has_wd);
-                    __stcs(ms4 + i, th[u]);
-                    __stcs(m4 + i, mm[u]);
-                    __stcs(v4 + i, vv[u]);
-                    if constexpr (kMixed) {
-                        uint2 p;
-                        p.x = pack_bf16x2_rn(th[u].x, th[u].y);
-                        p.y = pack_bf16x2_rn(th[u].z, th[u].w);
-                        reinterpret_cast<uint2*>(ch.param)[i] = p;
-                    }
-                }
-            }
-        }
-    }
-    for (uint32_t i = scalar_from + threadIdx.x; i < n; i += kThreads) {
+__device__ __forceinline__ void apply_scalar(const Chunk& ch, uint32_t from, uint32_t to,
+                                             uint32_t tid, uint32_t nthreads, const ApplyArgs& a,
+                                             const StepCoeffs& k, float lr_wd, bool has_wd) {
+    for (uint32_t i = from + tid; i < to; i += nthreads) {
         const float graw = kMixed ? bf16_bits_to_f32(static_cast<const uint16_t*>(ch.grad)[i])
                                   : static_cast<const float*>(ch.grad)[i];
         float th = ch.master[i], m = ch.m[i], v = ch.v[i];
-        adamw_elem(th, m, v, prep_grad(graw, k), k, lr_wd, has_wd);
+        adamw_elem(th, m, v, prep_grad(graw, k), a, k, lr_wd, has_wd);
         ch.master[i] = th;
         ch.m[i] = m;
         ch.v[i] = v;
@@ -261,14 +292,43 @@ __device__ __forceinline__ void apply_chunk(const Chunk& ch, const Coeffs& k) {
     }
 }
 
+// Visits the pipelined tiles of this CTA in order: vector chunks from the end
+// of the vector part of the table, grid-strided, each in kTile pieces. The
+// producer and the consumers walk exactly this sequence.
+template <typename F>
+__device__ __forceinline__ void for_each_tile(const Chunk* chunks, int n_vec, F&& f) {
+    uint32_t q = 0;
+    for (int c = n_vec - 1 - static_cast<int>(blockIdx.x); c >= 0; c -= gridDim.x) {
+        const Chunk ch = chunks[c];
+        for (uint32_t t0 = 0; t0 < ch.n; t0 += kTile, ++q) {
+            if (!f(ch, t0, min(static_cast<uint32_t>(kTile), ch.n - t0), q)) return;
+        }
+    }
+}
+
 template <bool kMixed>
-__global__ void __launch_bounds__(kThreads)
-k_apply(const Chunk* __restrict__ chunks, int n_chunks, Ctl* __restrict__ ctl, ApplyArgs a) {
-    __shared__ Coeffs s_k;
-    __shared__ int s_skip;
+__global__ void __launch_bounds__(kApplyThreads, 1)
+k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restrict__ ctl,
+        ApplyArgs a) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages];
+    __shared__ StepCoeffs s_k;
+    __shared__ int s_skip, s_found, s_err, s_drain_err;
+    // consumer-only failure flags, one per tile parity: written before the
+    // per-tile consumer barrier, read after it, so all consumers agree
+    __shared__ int s_cfail[2];
     __shared__ uint64_t s_t;
     __shared__ float s_norm;
-    __shared__ int s_found;
+    __shared__ uint32_t s_issued;
+
+    constexpr uint32_t kGradBytes = kMixed ? 2u : 4u;
+    constexpr uint32_t kVecElems = kVecBytes / kGradBytes;  // elements per 16 B of grad
+    constexpr uint32_t kStage = static_cast<uint32_t>(stage_bytes(kMixed));
+    constexpr uint32_t kOffMaster = kGradBytes * kTile, kOffM = kOffMaster + 4u * kTile,
+                       kOffV = kOffM + 4u * kTile;
+    constexpr int kConsumers = kConsumerWarps * 32;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         // Every CTA derives the same decision from the same bits; counters are
         // only read here and only written by the last CTA below.
@@ -287,31 +347,137 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, Ctl* __restrict__ ctl, A
         const uint64_t t = ctl->t + (skip ? 0u : 1u);
         const uint64_t ti = t < a.bc_len ? t : static_cast<uint64_t>(a.bc_len - 1);
         const float2 bc = a.bc[ti];
-        Coeffs k;
+        StepCoeffs k;
         k.inv = a.use_scaler ? __fdiv_rn(1.0f, ctl->scale) : 1.0f;
         k.coef = coef;
-        k.beta1 = a.beta1;
-        k.omb1 = __fsub_rn(1.0f, a.beta1);
-        k.beta2 = a.beta2;
-        k.omb2 = __fsub_rn(1.0f, a.beta2);
-        k.eps = a.eps;
         k.step_size = __fdiv_rn(a.lr, bc.x);  // adamw.cpp:130
         k.sqrt_bc2 = bc.y;
-        k.lr = a.lr;
         s_k = k;
         s_skip = skip;
         s_t = t;
         s_norm = norm;
         s_found = found;
+        s_err = 0;
+        s_drain_err = 0;
+        s_cfail[0] = s_cfail[1] = 0;
+        s_issued = 0;
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(smem_u32(&full_bar[s]), 1);
+            mbar_init(smem_u32(&empty_bar[s]), 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    const Coeffs k = s_k;
+    const StepCoeffs k = s_k;
+
     if (!s_skip) {
-        for (int c = n_chunks - 1 - static_cast<int>(blockIdx.x); c >= 0; c -= gridDim.x) {
-            apply_chunk<kMixed>(chunks[c], k);
+        if (warp == kConsumerWarps) {
+            // ---- producer: one thread keeps the ring full -------------------
+            if (lane == 0) {
+                for_each_tile(chunks, n_vec, [&](const Chunk& ch, uint32_t t0, uint32_t len,
+                                                 uint32_t q) {
+                    const uint32_t s = q % kStages;
+                    if (q >= kStages &&
+                        !mbar_wait(smem_u32(&empty_bar[s]), ((q / kStages) + 1) & 1, &s_err))
+                        return false;
+                    const uint32_t lv = len & ~(kVecElems - 1);
+                    const uint32_t fb = smem_u32(&full_bar[s]);
+                    mbar_expect_tx(fb, (kGradBytes + 12u) * lv);
+                    if (lv) {
+                        const uint32_t base = smem_u32(smem + s * kStage);
+                        bulk_load(base, static_cast<const char*>(ch.grad) + kGradBytes * t0,
+                                  kGradBytes * lv, fb);
+                        bulk_load(base + kOffMaster, ch.master + t0, 4u * lv, fb);
+                        bulk_load(base + kOffM, ch.m + t0, 4u * lv, fb);
+                        bulk_load(base + kOffV, ch.v + t0, 4u * lv, fb);
+                    }
+                    s_issued = q + 1;
+                    return true;
+                });
+            }
+        } else {
+            // ---- consumers ---------------------------------------------------
+            const uint32_t tid = threadIdx.x;
+            for_each_tile(chunks, n_vec, [&](const Chunk& ch, uint32_t t0, uint32_t len,
+                                             uint32_t q) {
+                const uint32_t s = q % kStages;
+                const bool ok = mbar_wait(smem_u32(&full_bar[s]), (q / kStages) & 1, &s_err);
+                if (!ok) s_cfail[q & 1] = 1;
+                const uint32_t lv = len & ~(kVecElems - 1);
+                unsigned char* st = smem + s * kStage;
+                if (ok) {
+                    const float lr_wd = __fmul_rn(a.lr, ch.wd);
+                    const bool has_wd = ch.wd != 0.0f;
+                    float4* sms = reinterpret_cast<float4*>(st + kOffMaster);
+                    float4* sm = reinterpret_cast<float4*>(st + kOffM);
+                    float4* sv = reinterpret_cast<float4*>(st + kOffV);
+                    const uint32_t nv = lv >> 2;
+                    for (uint32_t i = tid; i < nv; i += kConsumers) {
+                        float4 g;
+                        if constexpr (kMixed) {
+                            const uint2 q2 = reinterpret_cast<const uint2*>(st)[i];
+                            g = make_float4(bf16_lo(q2.x), bf16_hi(q2.x), bf16_lo(q2.y),
+                                            bf16_hi(q2.y));
+                        } else {
+                            g = reinterpret_cast<const float4*>(st)[i];
+                        }
+                        float4 th = sms[i], mm = sm[i], vv = sv[i];
+                        adamw_elem(th.x, mm.x, vv.x, prep_grad(g.x, k), a, k, lr_wd, has_wd);
+                        adamw_elem(th.y, mm.y, vv.y, prep_grad(g.y, k), a, k, lr_wd, has_wd);
+                        adamw_elem(th.z, mm.z, vv.z, prep_grad(g.z, k), a, k, lr_wd, has_wd);
+                        adamw_elem(th.w, mm.w, vv.w, prep_grad(g.w, k), a, k, lr_wd, has_wd);
+                        sms[i] = th;
+                        sm[i] = mm;
+                        sv[i] = vv;
+                        if constexpr (kMixed) {
+                            // the bf16 params take the grad's place in the stage
+                            uint2 p;
+                            p.x = pack_bf16x2_rn(th.x, th.y);
+                            p.y = pack_bf16x2_rn(th.z, th.w);
+                            reinterpret_cast<uint2*>(st)[i] = p;
+                        }
+                    }
+                    // the < 16-byte tail of the tile, straight from global memory
+                    apply_scalar<kMixed>(ch, t0 + lv, t0 + len, tid, kConsumers, a, k, lr_wd,
+                                         has_wd);
+                }
+                // make the stage's generic-proxy writes visible to the bulk store;
+                // after the barrier every consumer reads the same failure flag
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                consumers_sync<kConsumers>();
+                if (s_cfail[q & 1]) return false;
+                if (tid == 0) {
+                    if (lv) {
+                        const uint32_t base = smem_u32(st);
+                        if constexpr (kMixed)
+                            bulk_store(static_cast<uint16_t*>(ch.param) + t0, base, 2u * lv);
+                        bulk_store(ch.master + t0, base + kOffMaster, 4u * lv);
+                        bulk_store(ch.m + t0, base + kOffM, 4u * lv);
+                        bulk_store(ch.v + t0, base + kOffV, 4u * lv);
+                        bulk_commit();
+                        bulk_wait_read_all();  // the stage may be refilled after this
+                    }
+                    mbar_arrive(smem_u32(&empty_bar[s]));
+                }
+                return true;
+            });
+            if (tid == 0) bulk_wait_all();
+            // scalar chunks (misaligned heads, mixed-phase tensors)
+            for (int c = s_err ? n_chunks : n_vec + static_cast<int>(blockIdx.x); c < n_chunks; c += gridDim.x) {
+                const Chunk ch = chunks[c];
+                apply_scalar<kMixed>(ch, 0, ch.n, tid, kConsumers, a, k, __fmul_rn(a.lr, ch.wd),
+                                     ch.wd != 0.0f);
+            }
         }
     }
     __syncthreads();
+    if (s_err && threadIdx.x == kConsumerWarps * 32) {
+        // a wait timed out: let this CTA's own loads in flight land before exit
+        const uint32_t qi = s_issued;
+        for (uint32_t j = qi > kStages ? qi - kStages : 0; j < qi; ++j)
+            mbar_wait(smem_u32(&full_bar[j % kStages]), (j / kStages) & 1, &s_drain_err);
+        atomicOr(&ctl->error, 1);
+    }
     if (threadIdx.x == 0) {
         __threadfence();
         const unsigned prev = atomicAdd(&ctl->ticket_apply, 1u);
@@ -367,11 +533,20 @@ __global__ void k_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float sca
     ctl->skipped = skipped;
     ctl->scale = scale;
     ctl->tracker = tracker;
+    ctl->error = 0;
 }
 
 }  // namespace
 
 // --------------------------------------------------------------- launchers --
+
+cudaError_t prepare_kernels() {
+    cudaError_t e = cudaFuncSetAttribute(k_apply<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(apply_smem_bytes(true)));
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(k_apply<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(apply_smem_bytes(false)));
+}
 
 cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl* ctl,
                               double* partials, int grid, int use_scaler, double* out,
@@ -385,12 +560,14 @@ cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl*
     return cudaGetLastError();
 }
 
-cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, Ctl* ctl,
+cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
                          const ApplyArgs& args, int grid, cudaStream_t stream) {
     if (mixed)
-        k_apply<true><<<grid, kThreads, 0, stream>>>(chunks, n_chunks, ctl, args);
+        k_apply<true><<<grid, kApplyThreads, apply_smem_bytes(true), stream>>>(chunks, n_chunks,
+                                                                              n_vec, ctl, args);
     else
-        k_apply<false><<<grid, kThreads, 0, stream>>>(chunks, n_chunks, ctl, args);
+        k_apply<false><<<grid, kApplyThreads, apply_smem_bytes(false), stream>>>(
+            chunks, n_chunks, n_vec, ctl, args);
     return cudaGetLastError();
 }
 
@@ -427,9 +604,11 @@ int occupancy_grad_sumsq(bool bf16) {
 int occupancy_apply(bool mixed) {
     int n = 0;
     if (mixed)
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<true>, kThreads, 0);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<true>, kApplyThreads,
+                                                      apply_smem_bytes(true));
     else
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<false>, kThreads, 0);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<false>, kApplyThreads,
+                                                      apply_smem_bytes(false));
     return n > 0 ? n : 1;
 }
 

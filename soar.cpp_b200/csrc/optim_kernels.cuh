@@ -7,14 +7,19 @@
 
 namespace soarb {
 
-// Elements per chunk-table entry. A multiple of 4 (the vector width), large
-// enough that the per-chunk descriptor read (64 B) is noise next to the
-// 28 B/element the update streams (458 KB per full chunk).
+// Elements per chunk-table entry. A multiple of the tile, large enough that
+// the per-chunk descriptor read (64 B) is noise next to the 28 B/element the
+// update streams (458 KB per full chunk).
 constexpr uint32_t kChunkElems = 16384;
 
-// Chunk flag: every pointer of the chunk is vector aligned at its first
-// element (16 B for fp32 streams, 8 B for 4 x bf16), so the body runs on
-// 128-bit (fp32) / 64-bit (4 x bf16) loads and stores.
+// Vector alignment of a "vector" chunk: every stream starts on a 16-byte
+// boundary (8 bf16 or 4 fp32 elements), as bulk async copies require.
+constexpr uint32_t kVecBytes = 16;
+
+// Chunk flag: all pointers of the chunk are 16-byte aligned at its first
+// element. The host puts these chunks first in the table; the rest (short
+// heads of misaligned tensors, tensors whose param and grad have different
+// alignment phases) run a scalar path.
 constexpr uint32_t kChunkVec = 1u;
 
 // One contiguous run of at most kChunkElems elements of one tensor, with all
@@ -49,11 +54,13 @@ struct __align__(64) Ctl {
     double sumsq;           // single-GPU K1 output: sum of squared unscaled grads
     uint32_t ticket_sumsq;  // grid-reduction ticket of the sum-of-squares kernel
     uint32_t ticket_apply;  // completion ticket of the update kernel
+    int32_t error;          // nonzero: a pipeline wait timed out (the step is incomplete)
 };
 
 // Per-launch arguments of the update kernel.
 struct ApplyArgs {
     float lr, beta1, beta2, eps;
+    float omb1, omb2;     // 1 - beta1, 1 - beta2, rounded as the reference's float expressions
     float max_norm;       // > 0: clip by the global norm
     float pending_coef;   // coefficient from a standalone clip_grad_norm (1: none)
     float growth, backoff;
@@ -65,11 +72,25 @@ struct ApplyArgs {
     uint32_t bc_len;      // entries in bc; t >= bc_len uses bc[bc_len - 1]
 };
 
+// Update-kernel pipeline shape (measured best on B200 for the mixed layout:
+// 1024-element tiles, 6 stages, 12 consumer warps + 1 producer warp, 2 CTAs/SM).
+constexpr int kTile = 1024;
+constexpr int kStages = 6;
+constexpr int kConsumerWarps = 12;
+constexpr int kApplyThreads = (kConsumerWarps + 1) * 32;
+// bytes of one pipeline stage: grad tile + master, m, v tiles
+__host__ __device__ constexpr size_t stage_bytes(bool mixed) {
+    return (mixed ? 2u : 4u) * kTile + 12u * kTile;
+}
+__host__ __device__ constexpr size_t apply_smem_bytes(bool mixed) {
+    return stage_bytes(mixed) * kStages;
+}
+
 // Launchers (optim_kernels.cu). Each returns the launch status.
 cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl* ctl,
                               double* partials, int grid, int use_scaler, double* out,
                               cudaStream_t stream);
-cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, Ctl* ctl,
+cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
                          const ApplyArgs& args, int grid, cudaStream_t stream);
 cudaError_t launch_scale_grads_f32(const Chunk* chunks, int n_chunks, float coef, int grid,
                                    cudaStream_t stream);
@@ -77,6 +98,9 @@ cudaError_t launch_bf16_to_f32(const uint16_t* src, float* dst, uint64_t n,
                                cudaStream_t stream);
 cudaError_t launch_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float scale,
                                 int32_t tracker, cudaStream_t stream);
+
+// One-time per-process kernel attribute set-up (dynamic shared memory size).
+cudaError_t prepare_kernels();
 
 // Resident CTAs per SM of each kernel at its launch configuration.
 int occupancy_grad_sumsq(bool bf16);

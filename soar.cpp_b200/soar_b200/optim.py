@@ -48,7 +48,7 @@ class AdamWOpts(C.Structure):
 class StepInfo(C.Structure):
     _fields_ = [("step", C.c_uint64), ("skipped", C.c_uint64), ("grad_norm", C.c_float),
                 ("found_inf", C.c_int32), ("clip_coef", C.c_float), ("loss_scale", C.c_float),
-                ("growth_tracker", C.c_int32), ("lr", C.c_float)]
+                ("growth_tracker", C.c_int32), ("lr", C.c_float), ("error", C.c_int32)]
 
     def as_dict(self) -> dict:
         return {k: getattr(self, k) for k, _ in self._fields_}
