@@ -37,8 +37,9 @@ BYTES_PER_PARAM = 28          # algorithmic: read g 2 + master/m/v 12, write mas
 METRIC = "AdamW Gparams/s (fused ZeRO-1 optimizer step, 200M bf16-mixed params)"
 UNIT = "Gparams/s"
 # dram__bytes_read.sum + dram__bytes_write.sum of one k_apply launch on the full
-# 200M workload, from the ncu capture summarised in profiles/ (None until captured).
-APPLY_TRAFFIC_BYTES = None
+# 200M workload at N=1 (profiles/k_apply_config4.md: 2,801,499,392 read +
+# 2,740,448,512 written). Reported only for the workload it was measured on.
+APPLY_TRAFFIC_BYTES = {200_000_000: 5_541_947_904}
 
 
 def measured_peak_hbm() -> tuple[float, str]:
@@ -228,15 +229,16 @@ def run_ours(args):
 
     for _ in range(args.warmup):
         one_step()
-    torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
-
+    # the clock sampler starts before the barrier, so no rank enters the timed
+    # region while another is still setting it up
     clocks = ClockSampler(ROOT / "gpurun_out" / f"clocks_rank{rank}.csv") if rank == 0 else None
     if clocks:
         (ROOT / "gpurun_out").mkdir(exist_ok=True)
         clocks.start()
         time.sleep(0.3)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
     apply_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                 for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -314,7 +316,7 @@ def run_ours(args):
                          f"{16 * shard_params / 1e9:.1f} GB per rank)"},
         "roofline": {"bound": "hbm", "kernel": "k_apply", "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": APPLY_TRAFFIC_BYTES,
+                     "traffic": APPLY_TRAFFIC_BYTES.get(shard_params),
                      "algorithmic_bytes_per_launch": apply_bytes,
                      "apply_ms": apply_ms_max},
         "cpu_baseline": cpu,

@@ -174,33 +174,37 @@ void oracle_scaler_update(oracle_step_state* st, int found_inf, float growth_fac
     }
 }
 
-/* One complete optimizer step over a tensor list, as the fused device step
- * defines it:
- *   inv = 1/scale; g = unscale(grad) (exact for power-of-two scales);
- *   found_inf = any(!isfinite(g)); skip the whole step when the scaler is on
- *   and found_inf; norm/clip exactly as AdamW::clip_grad_norm on g (when
- *   max_norm > 0); AdamW::step on the fp32 master with the tensor's own wd;
- *   bf16 params = RNE(master) in the mixed layout; scaler update.
- * layout 0: params/grads are fp32 (params are the master, updated in place).
- * layout 1: params/grads are bf16, master holds the fp32 weights.
- * Tensors with a NULL grad are skipped (adamw.cpp:89-90,133-134).
- * scratch must hold max(numel) floats. Returns 1 when the step was skipped. */
-int oracle_step(int layout, int n_tensors, void** params, void** grads, float** master,
-                float** m, float** v, const uint64_t* numel, const float* wd,
-                float lr, float beta1, float beta2, float eps, float max_norm,
-                int use_scaler, float growth_factor, float backoff_factor,
-                int32_t growth_interval, oracle_step_state* st, float* scratch) {
-    float inv_scale = use_scaler ? 1.0f / st->scale : 1.0f;
+/* Sum of squares of the unscaled gradients of a tensor list, serial in tensor
+ * order (adamw.cpp:88-99 on the unscaled grads). *found_inf is set when any
+ * unscaled value is non-finite. scratch must hold max(numel) floats. */
+double oracle_grad_sumsq(int layout, int n_tensors, void** grads, const uint64_t* numel,
+                         float inv_scale, int* found_inf, float* scratch) {
     double sumsq = 0.0;
-    int found_inf = 0;
+    int found = 0;
     for (int k = 0; k < n_tensors; ++k) {
         if (!grads[k] || numel[k] == 0) continue;
         int f = layout == 1
                     ? oracle_unscale_bf16((const uint16_t*)grads[k], numel[k], inv_scale, scratch)
                     : oracle_unscale_f32((const float*)grads[k], numel[k], inv_scale, scratch);
-        found_inf |= f;
+        found |= f;
         sumsq = oracle_sumsq_f32(scratch, numel[k], sumsq);
     }
+    *found_inf = found;
+    return sumsq;
+}
+
+/* The update half of a step, given the global sum of squares (from this
+ * process alone, or summed over data-parallel ranks): skip decision, clip,
+ * AdamW with the tensor's own wd, bf16 write-back, scaler update.
+ * Returns 1 when the step was skipped. */
+int oracle_apply_with_sumsq(int layout, int n_tensors, void** params, void** grads,
+                            float** master, float** m, float** v, const uint64_t* numel,
+                            const float* wd, float lr, float beta1, float beta2, float eps,
+                            float max_norm, int use_scaler, float growth_factor,
+                            float backoff_factor, int32_t growth_interval, double sumsq,
+                            oracle_step_state* st, float* scratch) {
+    float inv_scale = use_scaler ? 1.0f / st->scale : 1.0f;
+    int found_inf = !isfinite(sumsq);
     float norm = oracle_norm_from_sumsq(sumsq);
     st->last_norm = norm;
     st->last_found_inf = found_inf;
@@ -230,6 +234,33 @@ int oracle_step(int layout, int n_tensors, void** params, void** grads, float** 
     }
     if (use_scaler) oracle_scaler_update(st, 0, growth_factor, backoff_factor, growth_interval);
     return 0;
+}
+
+/* One complete optimizer step over a tensor list, as the fused device step
+ * defines it:
+ *   inv = 1/scale; g = unscale(grad) (exact for power-of-two scales);
+ *   found_inf = any(!isfinite(g)); skip the whole step when the scaler is on
+ *   and found_inf; norm/clip exactly as AdamW::clip_grad_norm on g (when
+ *   max_norm > 0); AdamW::step on the fp32 master with the tensor's own wd;
+ *   bf16 params = RNE(master) in the mixed layout; scaler update.
+ * layout 0: params/grads are fp32 (params are the master, updated in place).
+ * layout 1: params/grads are bf16, master holds the fp32 weights.
+ * Tensors with a NULL grad are skipped (adamw.cpp:89-90,133-134).
+ * scratch must hold max(numel) floats. Returns 1 when the step was skipped.
+ * (found_inf is carried by the sum itself: any non-finite unscaled value
+ * makes the fp64 sum of squares non-finite.) */
+int oracle_step(int layout, int n_tensors, void** params, void** grads, float** master,
+                float** m, float** v, const uint64_t* numel, const float* wd,
+                float lr, float beta1, float beta2, float eps, float max_norm,
+                int use_scaler, float growth_factor, float backoff_factor,
+                int32_t growth_interval, oracle_step_state* st, float* scratch) {
+    float inv_scale = use_scaler ? 1.0f / st->scale : 1.0f;
+    int found_inf = 0;
+    double sumsq = oracle_grad_sumsq(layout, n_tensors, grads, numel, inv_scale, &found_inf,
+                                     scratch);
+    return oracle_apply_with_sumsq(layout, n_tensors, params, grads, master, m, v, numel, wd, lr,
+                                   beta1, beta2, eps, max_norm, use_scaler, growth_factor,
+                                   backoff_factor, growth_interval, sumsq, st, scratch);
 }
 
 /* ---- data-parallel reduce (ZeRO-1 reduce-scatter of bf16 gradients) ----- */

@@ -97,6 +97,17 @@ def _load_port() -> C.CDLL:
                                 C.c_float, C.c_float, C.c_int, C.c_float, C.c_float,
                                 C.c_int32, C.POINTER(StepState), _f32p]
     lib.oracle_reduce_avg_bf16.argtypes = [C.c_int, C.POINTER(C.c_void_p), C.c_size_t, _u16p]
+    lib.oracle_grad_sumsq.restype = C.c_double
+    lib.oracle_grad_sumsq.argtypes = [C.c_int, C.c_int, C.POINTER(C.c_void_p),
+                                      C.POINTER(C.c_uint64), C.c_float, C.POINTER(C.c_int), _f32p]
+    lib.oracle_apply_with_sumsq.restype = C.c_int
+    lib.oracle_apply_with_sumsq.argtypes = [C.c_int, C.c_int, C.POINTER(C.c_void_p),
+                                            C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                                            C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                                            C.POINTER(C.c_uint64), C.POINTER(C.c_float),
+                                            C.c_float, C.c_float, C.c_float, C.c_float,
+                                            C.c_float, C.c_int, C.c_float, C.c_float, C.c_int32,
+                                            C.c_double, C.POINTER(StepState), _f32p]
     return lib
 
 
@@ -185,6 +196,49 @@ class PortOptimizer:
             _ptrs(self.v), numel, wd, c.lr if lr is None else lr, c.beta1, c.beta2, c.eps,
             c.max_norm, int(c.use_scaler), c.growth_factor, c.backoff_factor,
             c.growth_interval, C.byref(self.state), self.scratch)
+
+
+class PortShard(PortOptimizer):
+    """The port oracle behind the data-parallel split API (grad_sumsq / apply
+    with rank-ordered partial sums), over numpy views of a rank's shards.
+    Stands in for the device optimizer in host-logic tests."""
+
+    def __init__(self, params, grads, wd, cfg: StepConfig, init_scale: float = 1.0):
+        super().__init__(params, wd, cfg, init_scale)
+        self.params = list(params)  # keep the caller's views: updates land in place
+        self.grads = list(grads)
+
+    def _inv(self):
+        return (np.float32(1.0) / np.float32(self.state.scale)) if self.cfg.use_scaler \
+            else np.float32(1.0)
+
+    def grad_sumsq_value(self) -> float:
+        n = len(self.params)
+        found = C.c_int()
+        return port().oracle_grad_sumsq(self.cfg.layout, n, _ptrs(self.grads),
+                                        (C.c_uint64 * n)(*self.numel), float(self._inv()),
+                                        C.byref(found), self.scratch)
+
+    def grad_sumsq(self, out_ptr: int, stream=None):
+        C.c_double.from_address(out_ptr).value = self.grad_sumsq_value()
+
+    def apply_sumsq(self, total: float, lr: float | None = None) -> int:
+        c = self.cfg
+        n = len(self.params)
+        return port().oracle_apply_with_sumsq(
+            c.layout, n, _ptrs(self.params), _ptrs(self.grads), _ptrs(self.master),
+            _ptrs(self.m), _ptrs(self.v), (C.c_uint64 * n)(*self.numel),
+            (C.c_float * n)(*self.wd.tolist()), c.lr if lr is None else lr, c.beta1, c.beta2,
+            c.eps, c.max_norm, int(c.use_scaler), c.growth_factor, c.backoff_factor,
+            c.growth_interval, total, C.byref(self.state), self.scratch)
+
+    def apply(self, parts_ptr: int, n_parts: int, stream=None):
+        total = 0.0
+        if n_parts:
+            parts = (C.c_double * n_parts).from_address(parts_ptr)
+            for x in parts:  # rank order, as the device sums them
+                total += x
+        return self.apply_sumsq(total)
 
 
 def reduce_avg_bf16(inputs: list[np.ndarray]) -> np.ndarray:

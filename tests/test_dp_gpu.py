@@ -1,0 +1,148 @@
+"""ZeRO-1 on 2 GPUs over NCCL, through the real driver and the CUDA optimizer.
+
+Each rank brings its own bf16 gradient; the step reduce-scatters it (NCCL,
+avg), runs the fused update on the rank's shard and all-gathers the params.
+The reduce-scatter has no reference counterpart and NCCL's summation order is
+its own, so parity is taken on what the optimizer received: every step the
+ranks' post-reduce-scatter shards are read back, reassembled, and fed to the
+single-process oracle. Checks: identical params on both ranks, skip /
+loss-scale / step sequences bit-exact, params within 1 bf16 ulp, and the
+reduce-scatter within bf16 rounding of the fp64 mean. Skipped below 2 GPUs."""
+import datetime
+import os
+import queue
+import socket
+import time
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+N = 3_000_017
+BUCKET = 1_000_000
+STEPS = 5
+INF_STEP = 3
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _grads(rank, step, scale):
+    from soar_b200 import synth
+    g = synth.normal(synth.seed_of(50, rank, step), N, 0.01) * np.float32(scale)
+    if step == INF_STEP and rank == 1:
+        g[123] = np.inf
+    return synth.to_bf16_bits(g.astype(np.float32))
+
+
+def _worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    import soar_b200 as sb
+    from soar_b200 import dp, synth
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        bf = lambda a: torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).cuda()
+        params = bf(synth.to_bf16_bits(synth.normal(synth.seed_of(51), N, 0.02)))
+        grads = torch.empty_like(params)
+
+        def make(sp, sg):
+            return sb.AdamW([sb.ParamGroup(sp, 0.01)], layout="bf16_mixed", max_grad_norm=1.0,
+                            loss_scaler=sb.LossScalerOptions(init_scale=1024.0,
+                                                             growth_interval=2),
+                            grads=sg, device=rank)
+
+        z = dp.ZeroOneAdamW(params, grads, BUCKET, make, dp.TorchComm())
+        scale = 1024.0
+        shards, hist = [], []
+        for t in range(1, STEPS + 1):
+            grads.copy_(bf(_grads(rank, t, scale)))
+            z.reduce_scatter()
+            shards.append(z.gshard.view(torch.int16).cpu().numpy().view(np.uint16).copy())
+            z.update(z.norm_partials())
+            z.all_gather()
+            info = z.opt.info()
+            scale = info.loss_scale
+            hist.append((info.skipped, info.loss_scale, info.step))
+        torch.cuda.synchronize()
+        out = params.view(torch.int16).cpu().numpy().view(np.uint16).copy()
+        q.put((rank, out, hist, shards, [(b.shard, b.own_size) for b in z.buckets]))
+        del z
+    finally:
+        dist.destroy_process_group()
+
+
+def test_zero1_two_gpus_nccl(oracle_mod):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    from soar_b200 import dp, synth
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    deadline = time.time() + 300
+    while len(res) < world and time.time() < deadline:
+        try:
+            r, *rest = q.get(timeout=2)
+            res[r] = rest
+        except queue.Empty:
+            if any(p.exitcode not in (None, 0) for p in procs):
+                break
+    for p in procs:
+        if p.is_alive() and len(res) < world:
+            p.terminate()
+        p.join(timeout=60)
+    assert len(res) == world, "a rank failed"
+    np.testing.assert_array_equal(res[0][0], res[1][0])
+    assert res[0][1] == res[1][1]
+
+    # reassemble each step's reduced gradient from the ranks' shards
+    o = oracle_mod
+    full_buckets = dp.plan_buckets(N, BUCKET, 1, 0)
+    p_full = synth.to_bf16_bits(synth.normal(synth.seed_of(51), N, 0.02))
+    views = [p_full[b.start:b.start + b.size] for b in full_buckets]
+    cfg = o.StepConfig(layout=1, max_norm=1.0, use_scaler=True, growth_interval=2)
+    ref = o.PortOptimizer(views, [0.01] * len(views), cfg, init_scale=1024.0)
+    ref.params = views
+    hist = []
+    for t in range(STEPS):
+        reduced = np.empty(N, np.uint16)
+        for b_full in full_buckets:
+            shard = -(-b_full.size // world)
+            for r in range(world):
+                off = sum(sh for sh, _ in res[r][3][:b_full.index])
+                lo = min(b_full.size, r * shard)
+                hi = min(b_full.size, (r + 1) * shard)
+                reduced[b_full.start + lo:b_full.start + hi] = res[r][2][t][off:off + hi - lo]
+        # the reduce-scatter itself: within bf16 rounding of the fp64 mean
+        ins = [synth.from_bf16_bits(_grads(r, t + 1, ref.state.scale)).astype(np.float64)
+               for r in range(world)]
+        mean = sum(ins) / world
+        got = synth.from_bf16_bits(reduced).astype(np.float64)
+        fin = np.isfinite(mean)
+        assert np.all(np.abs(got[fin] - mean[fin]) <= np.abs(mean[fin]) * 2.0 ** -7 + 1e-30)
+        ref.step([reduced[b.start:b.start + b.size] for b in full_buckets])
+        hist.append((ref.state.skipped, ref.state.scale, ref.state.t))
+    assert hist == res[0][1], (hist, res[0][1])
+    assert hist[INF_STEP - 1][0] == 1
+    diff = np.abs(res[0][0].astype(np.int32) - p_full.astype(np.int32))
+    assert diff.max() <= 1
