@@ -178,6 +178,55 @@ SOAR_API int soar_optim_loss_scale_ptr(void* handle, float** out_ptr);
 SOAR_API int soar_optim_grad_sumsq(void* handle, double* d_sumsq, void* stream);
 SOAR_API int soar_optim_apply(void* handle, const double* d_parts, int n_parts, void* stream);
 
+/* ---- Fused data-parallel step (ZeRO-1 over peer memory) -------------------
+   No counterpart in the reference, which has no distributed code. One process
+   per GPU; every rank's flat bf16 parameter and gradient buffers are allocated
+   with soar_ipc_alloc and opened by every other rank with soar_ipc_open (CUDA
+   IPC: the 64-byte handles travel between processes by any host channel, e.g.
+   torch.distributed), so all buffers are addressable from every GPU at
+   identical element offsets. */
+#define SOAR_IPC_HANDLE_BYTES 64
+
+SOAR_API int soar_ipc_alloc(size_t bytes, int device, void** out_ptr, void* out_handle);
+SOAR_API int soar_ipc_free(void* ptr, int device);
+SOAR_API int soar_ipc_open(const void* handle, int device, void** out_peer_ptr);
+SOAR_API int soar_ipc_close(void* peer_ptr, int device);
+
+/* One slice of the flat buffers owned by this rank: elements
+   [offset, offset + count), held by optimizer tensor `tensor`, whose param and
+   grad must be exactly that slice of this rank's buffers. */
+typedef struct soar_zero1_shard {
+    uint64_t offset;
+    uint64_t count;
+    int32_t tensor;
+} soar_zero1_shard;
+
+/* Binds a bf16-mixed optimizer over this rank's owned slices to the R
+   symmetric buffers (grad_bases[q] / param_bases[q]: rank q's buffers as seen
+   from this process; index `rank` is the local one). At most 8 ranks. */
+SOAR_API int soar_zero1_create(void* optim_handle, int rank, int world,
+                               void* const* grad_bases, void* const* param_bases,
+                               const soar_zero1_shard* shards, int n_shards, void** out_handle);
+
+/* Reduce-scatter fused with the norm pass: every owned element becomes the
+   average of the R ranks' gradients (fp32 sum in rank order, one multiply by
+   1/R, one bf16 rounding), written in place into the local gradient buffer;
+   *d_partial receives this rank's sum of squares of the unscaled averages.
+   Every rank's gradients must be complete before it runs (a barrier). */
+SOAR_API int soar_zero1_reduce_sumsq(void* zero1_handle, double* d_partial, void* stream);
+
+/* The update (as soar_optim_apply, with the R rank-ordered partials) fused
+   with the all-gather: each updated bf16 param tile is also written into
+   every peer's parameter buffer. Peers may read their parameters only after
+   every rank's call has completed (a barrier). */
+SOAR_API int soar_zero1_apply_allgather(void* zero1_handle, const double* d_parts, int n_parts,
+                                        void* stream);
+
+/* Nonzero in *out_error if a device-side wait of the reduce-scatter timed out
+   (synchronises the device). */
+SOAR_API int soar_zero1_error(void* zero1_handle, int* out_error);
+SOAR_API int soar_zero1_destroy(void* zero1_handle);
+
 /* Replaces CosineAnnealingLR (adamw.hpp:45-57, adamw.cpp:178-202): linear
    warmup, cosine decay to eta_min, eta_min past the end; each step() sets the
    bound optimizer's lr (host-side float math, the reference's expressions).

@@ -410,13 +410,14 @@ soarb::ApplyArgs apply_args(const Optim& o, const double* parts, int n_parts) {
     return a;
 }
 
-int apply_impl(Optim& o, const double* parts, int n_parts, cudaStream_t s) {
+int apply_impl(Optim& o, const double* parts, int n_parts, cudaStream_t s,
+               const soarb::AgArgs* ag = nullptr) {
     if (n_parts < 0 || (n_parts > 0 && !parts)) return fail("bad partial sums");
     int rc = ensure_bias_table(o);
     if (rc != SOAR_OK) return rc;
     const soarb::ApplyArgs a = apply_args(o, parts, n_parts);
     SOAR_CUDA_TRY(soarb::launch_apply(o.mixed, o.chunks, o.n_chunks, o.n_vec, o.ctl, a,
-                                      o.grid_apply, s));
+                                      o.grid_apply, s, ag));
     o.host_calls += 1;
     o.pending_coef = 1.0f;
     return SOAR_OK;
@@ -435,6 +436,30 @@ Optim* as_optim(void* h) { return static_cast<Optim*>(h); }
 namespace soarb {
 // Lets other translation units of the library report through soar_last_error().
 void record_error(const std::string& msg) { g_last_error = msg; }
+
+// The update with the fused data-parallel all-gather (zero1.cu).
+int optim_apply_allgather(void* optim, const double* parts, int n_parts, cudaStream_t stream,
+                          const AgArgs& ag) {
+    Optim& o = *as_optim(optim);
+    DeviceGuard g(o.device);
+    return apply_impl(o, parts, n_parts, stream, &ag);
+}
+
+// Tensor `index`'s param/grad/numel and the optimizer's layout, control block
+// and device (index -1: only the latter three).
+bool optim_tensor_info(void* optim, int index, void** param, void** grad, uint64_t* numel,
+                       bool* mixed, Ctl** ctl, int* device) {
+    Optim& o = *as_optim(optim);
+    *mixed = o.mixed;
+    *ctl = o.ctl;
+    *device = o.device;
+    if (index < 0) return index == -1;
+    if (static_cast<size_t>(index) >= o.tensors.size()) return false;
+    *param = o.tensors[index].param;
+    *grad = o.tensors[index].grad;
+    *numel = o.tensors[index].numel;
+    return true;
+}
 }  // namespace soarb
 
 extern "C" {

@@ -34,102 +34,10 @@
 // kernel records Ctl::error, stops issuing, waits (bounded) for its own copies
 // in flight and returns.
 #include "optim_kernels.cuh"
-
-#include <cuda_bf16.h>
+#include "pipeline.cuh"
 
 namespace soarb {
 namespace {
-
-// ------------------------------------------------------------ bf16 helpers --
-
-__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
-__device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) {
-    return __uint_as_float(static_cast<uint32_t>(h) << 16);
-}
-
-// Two fp32 -> packed bf16x2, round to nearest even (lo in the low half).
-__device__ __forceinline__ uint32_t pack_bf16x2_rn(float lo, float hi) {
-    uint32_t d;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
-    return d;
-}
-
-__device__ __forceinline__ uint16_t f32_to_bf16_rn(float x) {
-    return __bfloat16_as_ushort(__float2bfloat16_rn(x));
-}
-
-// -------------------------------------------------- mbarrier / bulk copies --
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ uint64_t global_timer_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
-
-// Bounded wait for the phase of `bar` with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* s_err) {
-    if (mbar_try(bar, parity)) return true;
-    const uint64_t t0 = global_timer_ns();
-    for (uint32_t i = 1;; ++i) {
-        if (mbar_try(bar, parity)) return true;
-        if ((i & 1023u) == 0) {
-            if (global_timer_ns() - t0 > kWaitLimitNs) {
-                atomicOr(s_err, 1);
-                return false;
-            }
-            if (*reinterpret_cast<volatile int*>(s_err)) return false;  // another thread gave up
-        }
-    }
-}
-// global -> shared, completes `bytes` of transaction on `bar`
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
-                                          uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-        "l"(src), "r"(bytes), "r"(bar)
-        : "memory");
-}
-// shared -> global, tracked by the issuing thread's bulk groups
-__device__ __forceinline__ void bulk_store(void* dst, uint32_t src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(src),
-                 "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read_all() {
-    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-}
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
-// Named barrier 1 over the kThreadsN consumer threads only.
-template <int kThreadsN>
-__device__ __forceinline__ void consumers_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kThreadsN) : "memory");
-}
 
 // -------------------------------------------------------------- reductions --
 
@@ -275,11 +183,13 @@ __device__ __forceinline__ float prep_grad(float graw, const StepCoeffs& k) {
     return __fmul_rn(__fmul_rn(graw, k.inv), k.coef);
 }
 
-// Elements [from, to) of a chunk, straight from global memory.
-template <bool kMixed>
+// Elements [from, to) of a chunk, straight from global memory. With kAg the
+// updated params are also written into every peer's parameter buffer.
+template <bool kMixed, bool kAg>
 __device__ __forceinline__ void apply_scalar(const Chunk& ch, uint32_t from, uint32_t to,
                                              uint32_t tid, uint32_t nthreads, const ApplyArgs& a,
-                                             const StepCoeffs& k, float lr_wd, bool has_wd) {
+                                             const StepCoeffs& k, float lr_wd, bool has_wd,
+                                             const AgArgs& ag) {
     for (uint32_t i = from + tid; i < to; i += nthreads) {
         const float graw = kMixed ? bf16_bits_to_f32(static_cast<const uint16_t*>(ch.grad)[i])
                                   : static_cast<const float*>(ch.grad)[i];
@@ -288,7 +198,21 @@ __device__ __forceinline__ void apply_scalar(const Chunk& ch, uint32_t from, uin
         ch.master[i] = th;
         ch.m[i] = m;
         ch.v[i] = v;
-        if constexpr (kMixed) static_cast<uint16_t*>(ch.param)[i] = f32_to_bf16_rn(th);
+        uint16_t pb = 0;
+        if constexpr (kMixed) {
+            pb = f32_to_bf16_rn(th);
+            static_cast<uint16_t*>(ch.param)[i] = pb;
+        }
+        if constexpr (kAg) {
+            const size_t off = static_cast<const char*>(ch.param) - ag.local_param_base;
+            for (int q = 0; q < ag.world; ++q) {
+                if (q == ag.rank) continue;
+                if constexpr (kMixed)
+                    reinterpret_cast<uint16_t*>(ag.peer_param_base[q] + off)[i] = pb;
+                else
+                    reinterpret_cast<float*>(ag.peer_param_base[q] + off)[i] = th;
+            }
+        }
     }
 }
 
@@ -306,10 +230,10 @@ __device__ __forceinline__ void for_each_tile(const Chunk* chunks, int n_vec, F&
     }
 }
 
-template <bool kMixed>
+template <bool kMixed, bool kAg>
 __global__ void __launch_bounds__(kApplyThreads, 1)
 k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restrict__ ctl,
-        ApplyArgs a) {
+        ApplyArgs a, AgArgs ag) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages];
     __shared__ StepCoeffs s_k;
@@ -438,8 +362,8 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                         }
                     }
                     // the < 16-byte tail of the tile, straight from global memory
-                    apply_scalar<kMixed>(ch, t0 + lv, t0 + len, tid, kConsumers, a, k, lr_wd,
-                                         has_wd);
+                    apply_scalar<kMixed, kAg>(ch, t0 + lv, t0 + len, tid, kConsumers, a, k,
+                                              lr_wd, has_wd, ag);
                 }
                 // make the stage's generic-proxy writes visible to the bulk store;
                 // after the barrier every consumer reads the same failure flag
@@ -454,6 +378,16 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                         bulk_store(ch.master + t0, base + kOffMaster, 4u * lv);
                         bulk_store(ch.m + t0, base + kOffM, 4u * lv);
                         bulk_store(ch.v + t0, base + kOffV, 4u * lv);
+                        if constexpr (kAg) {
+                            // the fused all-gather: the same param tile into every peer
+                            const size_t off = static_cast<const char*>(ch.param) -
+                                               ag.local_param_base +
+                                               static_cast<size_t>(kGradBytes) * t0;
+                            const uint32_t src = kMixed ? base : base + kOffMaster;
+                            for (int qq = 0; qq < ag.world; ++qq)
+                                if (qq != ag.rank)
+                                    bulk_store(ag.peer_param_base[qq] + off, src, kGradBytes * lv);
+                        }
                         bulk_commit();
                         bulk_wait_read_all();  // the stage may be refilled after this
                     }
@@ -465,10 +399,16 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
             // scalar chunks (misaligned heads, mixed-phase tensors)
             for (int c = s_err ? n_chunks : n_vec + static_cast<int>(blockIdx.x); c < n_chunks; c += gridDim.x) {
                 const Chunk ch = chunks[c];
-                apply_scalar<kMixed>(ch, 0, ch.n, tid, kConsumers, a, k, __fmul_rn(a.lr, ch.wd),
-                                     ch.wd != 0.0f);
+                apply_scalar<kMixed, kAg>(ch, 0, ch.n, tid, kConsumers, a, k,
+                                          __fmul_rn(a.lr, ch.wd), ch.wd != 0.0f, ag);
             }
         }
+    }
+    if constexpr (kAg) {
+        // peer writes (bulk stores, waited above, and scalar stores) are
+        // complete and visible system-wide before this CTA retires
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __threadfence_system();
     }
     __syncthreads();
     if (s_err && threadIdx.x == kConsumerWarps * 32) {
@@ -541,11 +481,17 @@ __global__ void k_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float sca
 // --------------------------------------------------------------- launchers --
 
 cudaError_t prepare_kernels() {
-    cudaError_t e = cudaFuncSetAttribute(k_apply<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(apply_smem_bytes(true)));
-    if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute(k_apply<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(apply_smem_bytes(false)));
+    cudaError_t e = cudaSuccess;
+    auto set = [&](auto kern, bool mixed) {
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(apply_smem_bytes(mixed)));
+    };
+    set(k_apply<true, false>, true);
+    set(k_apply<false, false>, false);
+    set(k_apply<true, true>, true);
+    set(k_apply<false, true>, false);
+    return e;
 }
 
 cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl* ctl,
@@ -561,13 +507,24 @@ cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl*
 }
 
 cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
-                         const ApplyArgs& args, int grid, cudaStream_t stream) {
-    if (mixed)
-        k_apply<true><<<grid, kApplyThreads, apply_smem_bytes(true), stream>>>(chunks, n_chunks,
-                                                                              n_vec, ctl, args);
-    else
-        k_apply<false><<<grid, kApplyThreads, apply_smem_bytes(false), stream>>>(
-            chunks, n_chunks, n_vec, ctl, args);
+                         const ApplyArgs& args, int grid, cudaStream_t stream, const AgArgs* ag) {
+    const AgArgs none{};
+    const size_t smem = apply_smem_bytes(mixed);
+    if (ag) {
+        if (mixed)
+            k_apply<true, true><<<grid, kApplyThreads, smem, stream>>>(chunks, n_chunks, n_vec,
+                                                                      ctl, args, *ag);
+        else
+            k_apply<false, true><<<grid, kApplyThreads, smem, stream>>>(chunks, n_chunks, n_vec,
+                                                                       ctl, args, *ag);
+    } else {
+        if (mixed)
+            k_apply<true, false><<<grid, kApplyThreads, smem, stream>>>(chunks, n_chunks, n_vec,
+                                                                       ctl, args, none);
+        else
+            k_apply<false, false><<<grid, kApplyThreads, smem, stream>>>(chunks, n_chunks, n_vec,
+                                                                        ctl, args, none);
+    }
     return cudaGetLastError();
 }
 
@@ -604,10 +561,10 @@ int occupancy_grad_sumsq(bool bf16) {
 int occupancy_apply(bool mixed) {
     int n = 0;
     if (mixed)
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<true>, kApplyThreads,
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<true, false>, kApplyThreads,
                                                       apply_smem_bytes(true));
     else
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<false>, kApplyThreads,
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<false, false>, kApplyThreads,
                                                       apply_smem_bytes(false));
     return n > 0 ? n : 1;
 }

@@ -72,6 +72,19 @@ struct ApplyArgs {
     uint32_t bc_len;      // entries in bc; t >= bc_len uses bc[bc_len - 1]
 };
 
+// Data-parallel all-gather fused into the update: after a tile of the rank's
+// shard is updated, its params (bf16 in the mixed layout, fp32 otherwise) are
+// also stored into every peer's parameter buffer at the same offset. The
+// buffers are symmetric: every rank's flat parameter buffer holds the whole
+// model at identical offsets.
+constexpr int kMaxRanks = 8;
+struct AgArgs {
+    int world;
+    int rank;
+    const char* local_param_base;        // this rank's flat parameter buffer
+    char* peer_param_base[kMaxRanks];    // every rank's flat parameter buffer (peer pointers)
+};
+
 // Update-kernel pipeline shape (measured best on B200 for the mixed layout:
 // 1024-element tiles, 6 stages, 12 consumer warps + 1 producer warp, 2 CTAs/SM).
 constexpr int kTile = 1024;
@@ -90,8 +103,10 @@ __host__ __device__ constexpr size_t apply_smem_bytes(bool mixed) {
 cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl* ctl,
                               double* partials, int grid, int use_scaler, double* out,
                               cudaStream_t stream);
+// ag == nullptr: plain update; otherwise the update with the fused all-gather.
 cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
-                         const ApplyArgs& args, int grid, cudaStream_t stream);
+                         const ApplyArgs& args, int grid, cudaStream_t stream,
+                         const AgArgs* ag = nullptr);
 cudaError_t launch_scale_grads_f32(const Chunk* chunks, int n_chunks, float coef, int grid,
                                    cudaStream_t stream);
 cudaError_t launch_bf16_to_f32(const uint16_t* src, float* dst, uint64_t n,

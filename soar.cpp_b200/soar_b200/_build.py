@@ -14,8 +14,8 @@ LIBDIR = ROOT / "lib"
 LIB = LIBDIR / "libsoar_optim.so"
 INCLUDE = ROOT.parent / "include"
 
-SOURCES = ["optim_kernels.cu", "optim_capi.cu", "noalloc_sumsq.cu"]
-HEADERS = ["optim_kernels.cuh"]
+SOURCES = ["optim_kernels.cu", "optim_capi.cu", "noalloc_sumsq.cu", "zero1.cu"]
+HEADERS = ["optim_kernels.cuh", "pipeline.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

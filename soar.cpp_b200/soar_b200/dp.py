@@ -17,9 +17,14 @@ One step:
   5. all-gather of every bucket's bf16 params.
 At R = 1 steps 1, 3 and 5 are identities and are skipped.
 
-The collectives go through a `Comm` object (torch.distributed by default), so
-the same driver runs over NCCL on GPUs and over gloo with a CPU stand-in
-optimizer in the host-logic tests.
+Two drivers:
+* ZeroOneAdamW -- the collectives of steps 1 and 5 are library calls through a
+  `Comm` object (torch.distributed / NCCL by default; gloo with a CPU stand-in
+  optimizer in the host-logic tests).
+* FusedZeroOneAdamW -- steps 1-2 are one kernel and steps 4-5 are one kernel
+  over peer memory (soar_zero1_*): the parameter and gradient buffers are
+  allocated by the library and opened by every rank through CUDA IPC; only the
+  8-byte partial all-gather and two 4-byte barriers go through NCCL.
 """
 from __future__ import annotations
 
@@ -162,3 +167,148 @@ class ZeroOneAdamW:
         parts = self.norm_partials()
         self.update(parts)
         self.all_gather()
+
+
+class _DevView:
+    def __init__(self, ptr: int, n: int, typestr: str):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+class FusedZeroOneAdamW:
+    """ZeRO-1 step with the reduce-scatter fused into the norm pass and the
+    all-gather fused into the update (see the module docstring).
+
+    `params` / `grads` are flat bf16 CUDA tensors viewing library-owned
+    symmetric buffers: fill `grads` with this rank's gradient before step();
+    after step() `params` holds the updated full model on every rank. The
+    rank's own slice of `grads` is overwritten with the reduced average.
+    make_optimizer(shard_params, shard_grads) -> soar_b200.AdamW (bf16_mixed).
+    init_params (n bf16 values, any device) is copied into `params` before the
+    optimizer is created, so its fp32 master weights start from them.
+    """
+
+    def __init__(self, n: int, bucket: int, make_optimizer, group=None, device: int | None = None,
+                 init_params=None):
+        import ctypes as C
+
+        import torch
+        import torch.distributed as dist
+
+        from . import optim as _o
+        self.torch, self.dist, self.group = torch, dist, group
+        self.lib = _o.lib()
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.device = torch.cuda.current_device() if device is None else device
+        self.n = n
+        self.buckets = plan_buckets(n, bucket, self.world, self.rank)
+        self._local, self._peers, self.zero1 = [], [], None
+        bases = {}
+        for name in ("grads", "params"):
+            ptr = C.c_void_p()
+            handle = (C.c_ubyte * _o.IPC_HANDLE_BYTES)()
+            _o._check(self.lib.soar_ipc_alloc(2 * n, self.device, C.byref(ptr), handle),
+                      "soar_ipc_alloc")
+            self._local.append(ptr.value)
+            handles = [None] * self.world
+            if self.world > 1:
+                dist.all_gather_object(handles, bytes(handle), group=group)
+            else:
+                handles = [bytes(handle)]
+            row = []
+            for q, h in enumerate(handles):
+                if q == self.rank:
+                    row.append(ptr.value)
+                    continue
+                peer = C.c_void_p()
+                buf = (C.c_ubyte * _o.IPC_HANDLE_BYTES).from_buffer_copy(h)
+                _o._check(self.lib.soar_ipc_open(buf, self.device, C.byref(peer)), "soar_ipc_open")
+                self._peers.append(peer.value)
+                row.append(peer.value)
+            bases[name] = row
+        dev = f"cuda:{self.device}"
+        self.grads = torch.as_tensor(_DevView(bases["grads"][self.rank], n, "<i2"),
+                                     device=dev).view(torch.bfloat16)
+        self.params = torch.as_tensor(_DevView(bases["params"][self.rank], n, "<i2"),
+                                      device=dev).view(torch.bfloat16)
+        if init_params is not None:
+            self.params.copy_(init_params)
+        mine = [b for b in self.buckets if b.own_size > 0]
+        self.shard_params = [self.params[b.own_start:b.own_start + b.own_size] for b in mine]
+        self.shard_grads = [self.grads[b.own_start:b.own_start + b.own_size] for b in mine]
+        self.opt = make_optimizer(self.shard_params, self.shard_grads)
+        shards = (_o.Zero1Shard * max(1, len(mine)))()
+        for i, b in enumerate(mine):
+            shards[i].offset, shards[i].count, shards[i].tensor = b.own_start, b.own_size, i
+        gb = (C.c_void_p * self.world)(*bases["grads"])
+        pb = (C.c_void_p * self.world)(*bases["params"])
+        h = C.c_void_p()
+        _o._check(self.lib.soar_zero1_create(self.opt.handle, self.rank, self.world, gb, pb,
+                                             shards, len(mine), C.byref(h)), "soar_zero1_create")
+        self.zero1 = h
+        self.part = torch.zeros(1, dtype=torch.float64, device=dev)
+        self.parts = torch.zeros(self.world, dtype=torch.float64, device=dev)
+        self.flag = torch.zeros(1, dtype=torch.float32, device=dev)
+
+    def _stream(self):
+        return self.torch.cuda.current_stream().cuda_stream
+
+    def barrier(self):
+        """Stream-ordered barrier: completes on this GPU only after every
+        rank's earlier work on its stream has completed."""
+        if self.world > 1:
+            self.dist.all_reduce(self.flag, group=self.group)
+
+    def reduce(self):
+        from . import optim as _o
+        _o._check(self.lib.soar_zero1_reduce_sumsq(self.zero1, self.part.data_ptr(),
+                                                    self._stream()), "soar_zero1_reduce_sumsq")
+
+    def gather_partials(self):
+        if self.world > 1:
+            self.dist.all_gather_into_tensor(self.parts, self.part, group=self.group)
+            return self.parts
+        return self.part
+
+    def update(self, parts):
+        from . import optim as _o
+        _o._check(self.lib.soar_zero1_apply_allgather(self.zero1, parts.data_ptr(), parts.numel(),
+                                                       self._stream()),
+                  "soar_zero1_apply_allgather")
+
+    def step(self):
+        self.barrier()                        # every rank's gradients are complete
+        self.reduce()                         # reduce-scatter + sum of squares
+        self.update(self.gather_partials())   # update + all-gather
+        self.barrier()                        # every peer's parameter writes landed
+
+    def error(self) -> int:
+        import ctypes as C
+
+        from . import optim as _o
+        out = C.c_int()
+        _o._check(self.lib.soar_zero1_error(self.zero1, C.byref(out)), "soar_zero1_error")
+        return out.value
+
+    def close(self):
+        if getattr(self, "zero1", None) is None and not getattr(self, "_local", None):
+            return
+        self.torch.cuda.synchronize(self.device)
+        if self.zero1 is not None:
+            self.lib.soar_zero1_destroy(self.zero1)
+            self.zero1 = None
+        if getattr(self, "opt", None) is not None:
+            self.opt.close()
+        for p in self._peers:
+            self.lib.soar_ipc_close(p, self.device)
+        self._peers = []
+        for p in self._local:
+            self.lib.soar_ipc_free(p, self.device)
+        self._local = []
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

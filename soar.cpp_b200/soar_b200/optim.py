@@ -87,8 +87,25 @@ SIGNATURES: dict[str, tuple] = {
     "soar_grad_sumsq_noalloc": (C.c_int, [C.POINTER(C.c_void_p), C.POINTER(C.c_uint64),
                                           C.c_int, C.c_int, C.c_float, C.c_void_p,
                                           C.c_void_p]),
+    "soar_ipc_alloc": (C.c_int, [C.c_size_t, C.c_int, C.POINTER(C.c_void_p), C.c_void_p]),
+    "soar_ipc_free": (C.c_int, [C.c_void_p, C.c_int]),
+    "soar_ipc_open": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_void_p)]),
+    "soar_ipc_close": (C.c_int, [C.c_void_p, C.c_int]),
+    "soar_zero1_create": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_void_p),
+                                    C.POINTER(C.c_void_p), C.c_void_p, C.c_int,
+                                    C.POINTER(C.c_void_p)]),
+    "soar_zero1_reduce_sumsq": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
+    "soar_zero1_apply_allgather": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
+    "soar_zero1_error": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "soar_zero1_destroy": (C.c_int, [C.c_void_p]),
     "soar_last_error": (C.c_char_p, []),
 }
+
+IPC_HANDLE_BYTES = 64
+
+
+class Zero1Shard(C.Structure):
+    _fields_ = [("offset", C.c_uint64), ("count", C.c_uint64), ("tensor", C.c_int32)]
 
 
 def library_path() -> Path:

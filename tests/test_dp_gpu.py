@@ -146,3 +146,108 @@ def test_zero1_two_gpus_nccl(oracle_mod):
     assert hist[INF_STEP - 1][0] == 1
     diff = np.abs(res[0][0].astype(np.int32) - p_full.astype(np.int32))
     assert diff.max() <= 1
+
+
+def _fused_worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    import soar_b200 as sb
+    from soar_b200 import dp, synth
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    fz = None
+    try:
+        bf = lambda a: torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).cuda()
+        p0 = bf(synth.to_bf16_bits(synth.normal(synth.seed_of(51), N, 0.02)))
+
+        def make(sp, sg):
+            return sb.AdamW([sb.ParamGroup(sp, 0.01)], layout="bf16_mixed", max_grad_norm=1.0,
+                            loss_scaler=sb.LossScalerOptions(init_scale=1024.0,
+                                                             growth_interval=2),
+                            grads=sg, device=rank)
+
+        fz = dp.FusedZeroOneAdamW(N, BUCKET, make, device=rank, init_params=p0)
+        scale = 1024.0
+        reduced, hist = [], []
+        for t in range(1, STEPS + 1):
+            fz.grads.copy_(bf(_grads(rank, t, scale)))
+            fz.barrier()
+            fz.reduce()
+            torch.cuda.synchronize()
+            mine = [fz.grads[b.own_start:b.own_start + b.own_size].view(torch.int16).cpu()
+                    .numpy().view(np.uint16).copy() for b in fz.buckets]
+            reduced.append(mine)
+            fz.update(fz.gather_partials())
+            fz.barrier()
+            info = fz.opt.info()
+            scale = info.loss_scale
+            hist.append((info.skipped, info.loss_scale, info.step))
+        torch.cuda.synchronize()
+        out = fz.params.view(torch.int16).cpu().numpy().view(np.uint16).copy()
+        q.put((rank, out, hist, reduced, fz.error()))
+    finally:
+        if fz is not None:
+            fz.close()
+        dist.destroy_process_group()
+
+
+def test_fused_zero1_two_gpus(oracle_mod):
+    """The fused path: reduce-scatter inside the norm kernel and all-gather
+    inside the update, over peer memory. Its reduce is defined exactly as the
+    oracle's (fp32 sum in rank order, one rounding), so the reduced shards are
+    checked bit-for-bit; the step against the single-process oracle."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    from soar_b200 import dp, synth
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    deadline = time.time() + 300
+    while len(res) < world and time.time() < deadline:
+        try:
+            r, *rest = q.get(timeout=2)
+            res[r] = rest
+        except queue.Empty:
+            if any(p.exitcode not in (None, 0) for p in procs):
+                break
+    for p in procs:
+        if p.is_alive() and len(res) < world:
+            p.terminate()
+        p.join(timeout=60)
+    assert len(res) == world, "a rank failed"
+    assert res[0][3] == 0 and res[1][3] == 0, "device-side wait timed out"
+    np.testing.assert_array_equal(res[0][0], res[1][0])
+    assert res[0][1] == res[1][1]
+
+    o = oracle_mod
+    full_buckets = dp.plan_buckets(N, BUCKET, 1, 0)
+    p_full = synth.to_bf16_bits(synth.normal(synth.seed_of(51), N, 0.02))
+    views = [p_full[b.start:b.start + b.size] for b in full_buckets]
+    cfg = o.StepConfig(layout=1, max_norm=1.0, use_scaler=True, growth_interval=2)
+    ref = o.PortOptimizer(views, [0.01] * len(views), cfg, init_scale=1024.0)
+    ref.params = views
+    hist = []
+    for t in range(STEPS):
+        avg = o.reduce_avg_bf16([_grads(r, t + 1, ref.state.scale) for r in range(world)])
+        for r in range(world):
+            for b, got in zip(dp.plan_buckets(N, BUCKET, world, r), res[r][2][t]):
+                np.testing.assert_array_equal(got, avg[b.own_start:b.own_start + b.own_size])
+        ref.step([avg[b.start:b.start + b.size] for b in full_buckets])
+        hist.append((ref.state.skipped, ref.state.scale, ref.state.t))
+    assert hist == res[0][1], (hist, res[0][1])
+    assert hist[INF_STEP - 1][0] == 1
+    diff = np.abs(res[0][0].astype(np.int32) - p_full.astype(np.int32))
+    assert diff.max() <= 1
