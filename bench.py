@@ -3,11 +3,13 @@
 Workload: 200M parameters, bf16 params and bf16 grads (N(0,1e-3) x loss scale
 65536, seeded per rank), fp32 master/m/v, 25M-element gradient buckets,
 global-norm clip 1.0, dynamic loss scaler, lr 1e-3, wd 0.01. At N GPUs each
-rank brings its own full 200M-element gradient; a step reduce-scatters it
-(NCCL, avg), runs the fused unscale/norm/clip/AdamW on the rank's 1/N shard and
-all-gathers the bf16 params. Unit: one parameter-gradient of one rank reduced
-and applied, so per-GPU work is fixed as N grows ("weak"); at N = 1 it is
-simply parameters updated per second.
+rank brings its own full 200M-element gradient; a step reduce-scatters it, runs
+the fused unscale/norm/clip/AdamW on the rank's 1/N shard and all-gathers the
+bf16 params -- by default with both collectives fused into the kernels over
+peer memory (--dp fused), or with NCCL around the kernels (--dp nccl). Unit:
+one parameter-gradient of one rank reduced and applied, so each GPU's input is
+fixed as N grows ("weak"); at N = 1 it is simply parameters updated per
+second.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
