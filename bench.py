@@ -61,6 +61,10 @@ def parse():
     ap.add_argument("--params", type=int, default=N_PARAMS)
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="config 5: flat 1M..2B params in both layouts, one JSON line each "
+                         "(not the headline line)")
+    ap.add_argument("--sweep-sizes", default="1000000,16000000,256000000,1000000000,2000000000")
     ap.add_argument("--dp", default="fused", choices=["fused", "nccl"],
                     help="N>1: collectives fused into the kernels over peer memory (default) "
                          "or NCCL reduce-scatter / all-gather around the kernels")
@@ -359,10 +363,62 @@ def run_ours(args):
     return 0
 
 
+def run_sweep(args):
+    """one flat tensor of N params, fp32 layout (fp32 param,
+    grad, m, v) and mixed layout (bf16 param and grad, fp32 master/m/v), no
+    clip or scaler (the plain update), 20 timed steps after 3 warm-up. Prints
+    one JSON line per (layout, N): Gparams/s and k_apply's achieved GB/s at
+    28 B/param against the measured HBM peak. Single GPU."""
+    import torch
+
+    import soar_b200 as sb
+    torch.cuda.set_device(0)
+    peak, peak_kind = measured_peak_hbm()
+    free = torch.cuda.mem_get_info()[0]
+    for layout in ("fp32", "bf16_mixed"):
+        for n in [int(x) for x in args.sweep_sizes.split(",")]:
+            need = 16 * n + (12 * n if layout == "bf16_mixed" else 8 * n)
+            if need > 0.9 * free:
+                print(json.dumps({"sweep": True, "layout": layout, "params": n,
+                                  "skipped": f"needs {need / 1e9:.1f} GB"}), flush=True)
+                continue
+            dt = torch.bfloat16 if layout == "bf16_mixed" else torch.float32
+            p = (torch.randn(n, device="cuda") * 0.02).to(dt)
+            g = (torch.randn(n, device="cuda") * 1e-3).to(dt)
+            opt = sb.AdamW([p], sb.AdamWOptions(lr=1e-3, weight_decay=0.01), layout=layout,
+                           grads=[g])
+            s = torch.cuda.current_stream()
+            for _ in range(3):
+                opt.step()
+            torch.cuda.synchronize()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(args.steps)]
+            for a, b in ev:
+                a.record(s)
+                opt.step()
+                b.record(s)
+            torch.cuda.synchronize()
+            ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+            gbs = BYTES_PER_PARAM * n / (ms * 1e-3) / 1e9
+            print(json.dumps({"sweep": True, "metric": "AdamW Gparams/s (config 5 sweep)",
+                              "layout": layout, "params": n, "steps": args.steps, "warmup": 3,
+                              "ms_per_step": ms, "value": n / (ms * 1e-3) / 1e9,
+                              "unit": "Gparams/s", "achieved_gbs": gbs, "peak_gbs": peak,
+                              "peak_kind": peak_kind, "frac": gbs / peak,
+                              "l2": "larger than L2" if 16 * n > 126e6 else "fits in L2"}),
+                  flush=True)
+            opt.close()
+            del p, g, opt
+            torch.cuda.empty_cache()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.sweep:
+        return run_sweep(args)
     return run_ours(args)
 
 

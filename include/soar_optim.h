@@ -57,7 +57,12 @@ enum soar_layout {
 };
 
 /* Which optimizer-owned state array of a tensor (soar_optim_state_ptr & co). */
-enum soar_state_kind { SOAR_STATE_MASTER = 0, SOAR_STATE_M = 1, SOAR_STATE_V = 2 };
+enum soar_state_kind {
+    SOAR_STATE_MASTER = 0,
+    SOAR_STATE_M = 1,
+    SOAR_STATE_V = 2,
+    SOAR_STATE_EMA = 3  /* weight-EMA shadow, when enabled */
+};
 
 /* One parameter tensor (the reference's TensorPtr list entry). */
 typedef struct soar_tensor_desc {
@@ -161,6 +166,31 @@ SOAR_API int soar_optim_state_ptr(void* handle, int index, int kind, void** out_
 /* Synchronous host copies of one tensor's state (checkpointing, tests). */
 SOAR_API int soar_optim_read_state(void* handle, int index, int kind, float* host_dst);
 SOAR_API int soar_optim_write_state(void* handle, int index, int kind, const float* host_src);
+
+/* Optimizer-state checkpoint. No counterpart in the reference, whose
+   checkpoints hold model weights only (src/nn/soar_model.cpp:427-523), so a
+   resumed run restarts Adam's moments and bias correction. Writes/reads a
+   SOAR file (magic 'SOAR', version 2) in the reference's weight-record layout:
+   records "optim.master.<i>", "optim.m.<i>", "optim.v.<i>" (fp32, tensor i of
+   the list; plus "optim.ema.<i>" when the weight EMA is on) and "optim.counters" (step count, skipped steps, loss scale,
+   growth tracker, lr). The reference's weight loader skips these names. Load
+   needs an optimizer created over the same tensor list; in the mixed layout
+   it also rewrites the bf16 params from the restored master. Synchronous. */
+SOAR_API int soar_optim_save_state(void* handle, const char* path);
+SOAR_API int soar_optim_load_state(void* handle, const char* path, void* stream);
+
+/* Weight EMA fused into the update: replaces soar::utils::ModelEMA
+   (include/soar/utils/ema.hpp:10-66). enable allocates the shadow and copies
+   the current fp32 weights into it (init_shadow, ema.hpp:52-58); from then on
+   every applied step also computes shadow = decay*shadow + (1-decay)*weight
+   (update, ema.hpp:18-28) inside the update kernel, on the fp32 master
+   weights (the fp32 params in the FP32 layout), for +8 bytes per param.
+   Skipped steps leave the shadow unchanged. Calling enable again resets the
+   shadow to the current weights and sets a new decay. */
+SOAR_API int soar_optim_enable_ema(void* handle, float decay, void* stream);
+/* ModelEMA::apply_to (ema.hpp:31-38): the weights become the shadow (master
+   and bf16 params in the mixed layout). */
+SOAR_API int soar_optim_ema_apply_to(void* handle, void* stream);
 
 /* Device address of the live loss scale (fp32), for scaling the loss on the
    device without a host round trip. */

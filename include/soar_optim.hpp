@@ -1,0 +1,170 @@
+// soar_optim.hpp -- C++ API of the B200 optimizer step, source-compatible with
+// the reference's soar::optim::AdamW / AdamWOptions / CosineAnnealingLR
+// (include/soar/optim/adamw.hpp:10-57). Header-only over the C-ABI in
+// soar_optim.h; link libsoar_optim.so.
+//
+// The constructor takes the reference's own parameter list type: any
+// std::vector<P> whose elements behave like the reference's TensorPtr
+// (p->numel(), p->cuda_data(), p->grad() returning a pointer-like with
+// cuda_data(); include/soar/tensor/tensor.hpp:47,80,95). Params must be on the
+// GPU (the reference keeps a host copy and a CUDA copy; this step reads and
+// writes only the CUDA copy). As in the reference, params without a gradient
+// are skipped and the optimizer owns m and v (adamw.hpp:33-39).
+//
+// Differences, all additive: step()/zero_grad() take an optional stream; the
+// optimizer is move-only (the reference's Trainer holds it by value,
+// trainer.hpp:100, and moves it in); errors throw std::runtime_error carrying
+// soar_last_error() where the reference would throw DeviceError.
+#pragma once
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "soar_optim.h"
+
+namespace soar::optim {
+
+struct AdamWOptions {  // adamw.hpp:10-16, same fields and defaults
+    float lr{1e-3f};
+    float beta1{0.9f};
+    float beta2{0.999f};
+    float eps{1e-8f};
+    float weight_decay{1e-2f};
+};
+
+// Extensions with no reference counterpart (mixed precision, fused clip,
+// loss scaler). Defaults reproduce the reference's fp32 behaviour.
+struct AdamWExtOptions {
+    int layout{SOAR_LAYOUT_FP32};
+    float max_grad_norm{0.0f};
+    bool use_loss_scaler{false};
+    float init_scale{65536.0f};
+    float growth_factor{2.0f};
+    float backoff_factor{0.5f};
+    int growth_interval{200};
+    int device{0};
+};
+
+namespace detail {
+inline void check(int rc, const char* what) {
+    if (rc != SOAR_OK) throw std::runtime_error(std::string(what) + ": " + soar_last_error());
+}
+}  // namespace detail
+
+class AdamW {
+public:
+    // AdamW(std::vector<TensorPtr> params, AdamWOptions options = {}) (adamw.hpp:23)
+    template <class P>
+    explicit AdamW(const std::vector<P>& params, AdamWOptions options = {},
+                   AdamWExtOptions ext = {}) {
+        std::vector<soar_tensor_desc> d;
+        d.reserve(params.size());
+        for (const auto& p : params) {
+            soar_tensor_desc t{};
+            if (p) {
+                t.param = p->cuda_data();
+                auto g = p->grad();
+                t.grad = g ? g->cuda_data() : nullptr;
+                t.numel = static_cast<uint64_t>(p->numel());
+            }
+            t.weight_decay = options.weight_decay;
+            d.push_back(t);
+        }
+        create(d, options, ext);
+    }
+
+    // Raw descriptors (per-tensor weight decay = parameter groups).
+    AdamW(const std::vector<soar_tensor_desc>& tensors, AdamWOptions options,
+          AdamWExtOptions ext) {
+        create(tensors, options, ext);
+    }
+
+    AdamW(AdamW&& o) noexcept : h_(std::exchange(o.h_, nullptr)) {}
+    AdamW& operator=(AdamW&& o) noexcept {
+        if (this != &o) {
+            reset();
+            h_ = std::exchange(o.h_, nullptr);
+        }
+        return *this;
+    }
+    AdamW(const AdamW&) = delete;
+    AdamW& operator=(const AdamW&) = delete;
+    ~AdamW() { reset(); }
+
+    void step(void* stream = nullptr) { detail::check(soar_optim_step(h_, stream), "step"); }
+    void zero_grad(void* stream = nullptr) {
+        detail::check(soar_optim_zero_grad(h_, stream), "zero_grad");
+    }
+    float clip_grad_norm(float max_norm, void* stream = nullptr) {
+        float n = 0.0f;
+        detail::check(soar_optim_clip_grad_norm(h_, max_norm, &n, stream), "clip_grad_norm");
+        return n;
+    }
+    void set_lr(float lr) noexcept { soar_optim_set_lr(h_, lr); }
+    [[nodiscard]] float get_lr() const noexcept {
+        float lr = 0.0f;
+        soar_optim_get_lr(h_, &lr);
+        return lr;
+    }
+
+    [[nodiscard]] soar_step_info info(void* stream = nullptr) const {
+        soar_step_info i{};
+        detail::check(soar_optim_get_info(h_, &i, stream), "get_info");
+        return i;
+    }
+    [[nodiscard]] void* handle() const noexcept { return h_; }
+
+private:
+    void create(const std::vector<soar_tensor_desc>& d, const AdamWOptions& o,
+                const AdamWExtOptions& ext) {
+        soar_adamw_opts c;
+        soar_adamw_default_opts(&c);
+        c.lr = o.lr;
+        c.beta1 = o.beta1;
+        c.beta2 = o.beta2;
+        c.eps = o.eps;
+        c.weight_decay = o.weight_decay;
+        c.layout = ext.layout;
+        c.max_grad_norm = ext.max_grad_norm;
+        c.use_loss_scaler = ext.use_loss_scaler ? 1 : 0;
+        c.init_scale = ext.init_scale;
+        c.growth_factor = ext.growth_factor;
+        c.backoff_factor = ext.backoff_factor;
+        c.growth_interval = ext.growth_interval;
+        c.device = ext.device;
+        detail::check(soar_optim_create(d.data(), static_cast<int>(d.size()), &c, &h_), "create");
+    }
+    void reset() noexcept {
+        if (h_) soar_optim_destroy(h_);
+        h_ = nullptr;
+    }
+    void* h_{nullptr};
+};
+
+// CosineAnnealingLR(AdamW&, total_steps, eta_min = 1e-6f, warmup_steps = 0)
+// (adamw.hpp:45-57). Bound to the optimizer's handle, so it follows the
+// optimizer across moves (the reference binds a reference to the object).
+class CosineAnnealingLR {
+public:
+    CosineAnnealingLR(AdamW& optimizer, size_t total_steps, float eta_min = 1e-6f,
+                      size_t warmup_steps = 0) {
+        detail::check(soar_cosine_create(optimizer.handle(), total_steps, eta_min, warmup_steps,
+                                         &h_),
+                      "cosine_create");
+    }
+    CosineAnnealingLR(CosineAnnealingLR&& o) noexcept : h_(std::exchange(o.h_, nullptr)) {}
+    CosineAnnealingLR(const CosineAnnealingLR&) = delete;
+    CosineAnnealingLR& operator=(const CosineAnnealingLR&) = delete;
+    ~CosineAnnealingLR() {
+        if (h_) soar_cosine_destroy(h_);
+    }
+    void step() { detail::check(soar_cosine_step(h_), "cosine_step"); }
+
+private:
+    void* h_{nullptr};
+};
+
+}  // namespace soar::optim

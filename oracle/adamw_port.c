@@ -263,6 +263,12 @@ int oracle_step(int layout, int n_tensors, void** params, void** grads, float** 
                                    backoff_factor, growth_interval, sumsq, st, scratch);
 }
 
+/* ModelEMA::update (reference include/soar/utils/ema.hpp:18-28) over one
+ * weight array: shadow = decay * shadow + (1 - decay) * weight. */
+void oracle_ema_update(float* shadow, const float* weight, size_t n, float decay) {
+    for (size_t j = 0; j < n; ++j) shadow[j] = decay * shadow[j] + (1.0f - decay) * weight[j];
+}
+
 /* ---- data-parallel reduce (ZeRO-1 reduce-scatter of bf16 gradients) ----- */
 
 /* Average of R bf16 gradient buffers, summed in fp32 in rank order 0..R-1,

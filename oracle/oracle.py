@@ -97,6 +97,7 @@ def _load_port() -> C.CDLL:
                                 C.c_float, C.c_float, C.c_int, C.c_float, C.c_float,
                                 C.c_int32, C.POINTER(StepState), _f32p]
     lib.oracle_reduce_avg_bf16.argtypes = [C.c_int, C.POINTER(C.c_void_p), C.c_size_t, _u16p]
+    lib.oracle_ema_update.argtypes = [_f32p, _f32p, C.c_size_t, C.c_float]
     lib.oracle_grad_sumsq.restype = C.c_double
     lib.oracle_grad_sumsq.argtypes = [C.c_int, C.c_int, C.POINTER(C.c_void_p),
                                       C.POINTER(C.c_uint64), C.c_float, C.POINTER(C.c_int), _f32p]
@@ -184,6 +185,17 @@ class PortOptimizer:
         self.v = [np.zeros(n, np.float32) for n in self.numel]
         self.state = StepState(scale=init_scale if cfg.use_scaler else 1.0)
         self.scratch = np.zeros(max(self.numel + [1]), np.float32)
+        self.ema = None
+        self.ema_decay = 0.0
+
+    def weights(self, i: int) -> np.ndarray:
+        """fp32 weights of tensor i (the master in the mixed layout)."""
+        return self.master[i] if self.cfg.layout == 1 else self.params[i]
+
+    def enable_ema(self, decay: float):
+        """ModelEMA: the shadow starts as a copy of the weights (ema.hpp:52-58)."""
+        self.ema = [self.weights(i).astype(np.float32).copy() for i in range(len(self.params))]
+        self.ema_decay = decay
 
     def step(self, grads, lr: float | None = None) -> int:
         c = self.cfg
@@ -191,11 +203,18 @@ class PortOptimizer:
         grads = [None if g is None else np.ascontiguousarray(g) for g in grads]
         numel = (C.c_uint64 * n)(*self.numel)
         wd = (C.c_float * n)(*self.wd.tolist())
-        return port().oracle_step(
+        skipped = port().oracle_step(
             c.layout, n, _ptrs(self.params), _ptrs(grads), _ptrs(self.master), _ptrs(self.m),
             _ptrs(self.v), numel, wd, c.lr if lr is None else lr, c.beta1, c.beta2, c.eps,
             c.max_norm, int(c.use_scaler), c.growth_factor, c.backoff_factor,
             c.growth_interval, C.byref(self.state), self.scratch)
+        if self.ema is not None and not skipped:
+            # the fused EMA follows the weights the step updated (tensors with a grad)
+            for i, g in enumerate(grads):
+                if g is not None and self.numel[i]:
+                    port().oracle_ema_update(self.ema[i], np.ascontiguousarray(self.weights(i)),
+                                             self.numel[i], self.ema_decay)
+        return skipped
 
 
 class PortShard(PortOptimizer):
@@ -334,6 +353,42 @@ class RefAdamW:
     def set_moment(self, idx: int, which: int, val: np.ndarray):
         assert ref().soar_ref_adamw_set_moment(self.h, idx, which,
                                                np.ascontiguousarray(val, np.float32)) == 0
+
+
+class RefEma:
+    """The reference's soar::utils::ModelEMA over numpy fp32 weights (in place)."""
+
+    def __init__(self, params, decay):
+        lib = ref()
+        if not hasattr(lib, "_ema_bound"):
+            lib.soar_ref_ema_create.restype = C.c_void_p
+            lib.soar_ref_ema_create.argtypes = [C.POINTER(C.c_void_p), C.POINTER(C.c_uint64),
+                                                C.c_int, C.c_float]
+            for nm in ("update", "apply_to", "destroy"):
+                getattr(lib, f"soar_ref_ema_{nm}").argtypes = [C.c_void_p]
+            lib.soar_ref_ema_shadow.restype = C.c_int
+            lib.soar_ref_ema_shadow.argtypes = [C.c_void_p, C.c_int, _f32p]
+            lib._ema_bound = True
+        self.params = params
+        n = len(params)
+        self.h = lib.soar_ref_ema_create(_ptrs(params), (C.c_uint64 * n)(*[p.size for p in params]),
+                                         n, decay)
+
+    def update(self):
+        ref().soar_ref_ema_update(self.h)
+
+    def apply_to(self):
+        ref().soar_ref_ema_apply_to(self.h)
+
+    def shadow(self, i) -> np.ndarray:
+        out = np.empty(self.params[i].size, np.float32)
+        assert ref().soar_ref_ema_shadow(self.h, i, out) == 0
+        return out
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            ref().soar_ref_ema_destroy(self.h)
+            self.h = None
 
 
 class RefCosine:

@@ -23,12 +23,19 @@
 #define private public
 #include <soar/optim/adamw.hpp>  // the reference header, unmodified
 #undef private
+#include <soar/nn/module.hpp>    // the stand-in (oracle/standin)
+#include <soar/utils/ema.hpp>    // the reference header, unmodified
 
 namespace {
 
 struct RefOptim {
     std::vector<soar::TensorPtr> params;
     std::unique_ptr<soar::optim::AdamW> opt;
+};
+
+struct RefEma {
+    std::shared_ptr<soar::nn::Module> model;
+    std::unique_ptr<soar::utils::ModelEMA> ema;
 };
 
 struct RefSched {
@@ -107,5 +114,32 @@ void* soar_ref_cosine_create(void* h, uint64_t total_steps, float eta_min, uint6
 void soar_ref_cosine_step(void* s) { static_cast<RefSched*>(s)->sched->step(); }
 
 void soar_ref_cosine_destroy(void* s) { delete static_cast<RefSched*>(s); }
+
+// The reference's ModelEMA over numpy weight buffers (viewed in place).
+void* soar_ref_ema_create(float** params, const uint64_t* numel, int n, float decay) {
+    std::vector<soar::TensorPtr> ps;
+    for (int i = 0; i < n; ++i)
+        ps.push_back(std::make_shared<soar::Tensor>(params[i], static_cast<size_t>(numel[i])));
+    auto* h = new RefEma();
+    h->model = std::make_shared<soar::nn::Module>(ps);
+    h->ema = std::make_unique<soar::utils::ModelEMA>(h->model, decay);
+    return h;
+}
+void soar_ref_ema_update(void* h) {
+    auto* r = static_cast<RefEma*>(h);
+    r->ema->update(r->model);
+}
+void soar_ref_ema_apply_to(void* h) {
+    auto* r = static_cast<RefEma*>(h);
+    r->ema->apply_to(r->model);
+}
+int soar_ref_ema_shadow(void* h, int idx, float* out) {
+    auto* r = static_cast<RefEma*>(h);
+    const auto& sh = r->ema->shadow_params();
+    if (idx < 0 || static_cast<size_t>(idx) >= sh.size()) return -1;
+    std::memcpy(out, sh[idx]->data(), sh[idx]->numel() * sizeof(float));
+    return 0;
+}
+void soar_ref_ema_destroy(void* h) { delete static_cast<RefEma*>(h); }
 
 }  // extern "C"

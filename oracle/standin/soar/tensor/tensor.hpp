@@ -15,6 +15,7 @@
 #include <cstddef>
 #include <cstring>
 #include <memory>
+#include <vector>
 
 namespace soar {
 
@@ -24,6 +25,12 @@ using TensorPtr = std::shared_ptr<Tensor>;
 class Tensor {
 public:
     Tensor(float* data, size_t numel) : data_(data), numel_(numel) {}
+    explicit Tensor(size_t numel) : own_(numel, 0.0f), data_(own_.data()), numel_(numel) {}
+
+    static TensorPtr create(size_t shape, bool /*requires_grad*/) {
+        return std::make_shared<Tensor>(shape);
+    }
+    [[nodiscard]] size_t shape() const noexcept { return numel_; }
 
     [[nodiscard]] size_t numel() const noexcept { return numel_; }
     [[nodiscard]] float* data() noexcept { return data_; }
@@ -46,6 +53,7 @@ public:
     }
 
 private:
+    std::vector<float> own_;
     float* data_;
     size_t numel_;
     TensorPtr grad_;

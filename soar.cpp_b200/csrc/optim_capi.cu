@@ -8,6 +8,8 @@
 // kernel launches with no host work beyond filling the launch arguments.
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
+#include <map>
 #include <cstdint>
 #include <cstring>
 #include <new>
@@ -82,12 +84,15 @@ struct Optim {
     soarb::Ctl* ctl = nullptr;
     double* sumsq_scratch = nullptr;
 
+    float* ema = nullptr;        // weight-EMA shadow (separate allocation, state layout)
+    float ema_decay = 0.0f;
     float2* bc = nullptr;        // separate allocation (it can grow)
     uint32_t bc_len = 0;
     bool bc_converged = false;
 
     int grid_sumsq = 1;
     int grid_apply = 1;
+    uint32_t chunk_elems = soarb::kChunkElems;  // adaptive: see choose_chunk_elems
     std::vector<soarb::Chunk> host_chunks;
 };
 
@@ -160,8 +165,19 @@ int upload_bias_table(Optim& o, uint32_t len) {
 // A tensor whose param and grad phases differ runs the scalar path. Vector
 // chunks go first in the table (they feed the bulk-copy pipeline), scalar
 // chunks after them.
+// Chunk length: about 8 chunks per update CTA so small tensor lists still
+// spread over every SM and the grid-stride tail stays short, a power of two
+// between one tile and kChunkElems (large lists keep kChunkElems).
+uint32_t choose_chunk_elems(uint64_t total_elems, int grid) {
+    const uint64_t target = total_elems / (8ull * static_cast<uint64_t>(std::max(grid, 1)));
+    uint32_t c = soarb::kChunkElems;
+    while (c > static_cast<uint32_t>(soarb::kTile) && c > target) c >>= 1;
+    return c;
+}
+
 void build_chunks(Optim& o) {
     const size_t eb = elem_bytes(o);
+    const uint32_t kChunk = o.chunk_elems;
     std::vector<soarb::Chunk> vec, scalar;
     uint64_t cursor = 0;
     for (size_t ti = 0; ti < o.tensors.size(); ++ti) {
@@ -173,8 +189,7 @@ void build_chunks(Optim& o) {
         const bool vec_ok = t.grad && t.numel > 0 && pphase == gphase;
         uint64_t h16 = 0, e0 = 0;  // first 16-byte aligned index, first boundary index
         if (vec_ok) {
-            const uint64_t align_elems =
-                t.numel >= 8ull * soarb::kChunkElems ? soarb::kChunkElems : soarb::kTile;
+            const uint64_t align_elems = t.numel >= 8ull * kChunk ? kChunk : soarb::kTile;
             const uint64_t ab = align_elems * eb;
             const uint64_t h16_raw = ((soarb::kVecBytes - ga % soarb::kVecBytes) % soarb::kVecBytes) / eb;
             const uint64_t e0_raw = ((ab - ga % ab) % ab) / eb;  // >= h16_raw, same phase mod 16 B
@@ -204,8 +219,8 @@ void build_chunks(Optim& o) {
             (is_vec ? vec : scalar).push_back(c);
         };
         auto add_run = [&](uint64_t from, uint64_t to, bool is_vec) {
-            for (uint64_t s = from; s < to; s += soarb::kChunkElems)
-                add(s, std::min<uint64_t>(soarb::kChunkElems, to - s), is_vec);
+            for (uint64_t s = from; s < to; s += kChunk)
+                add(s, std::min<uint64_t>(kChunk, to - s), is_vec);
         };
         if (!vec_ok) {
             add_run(0, t.numel, false);
@@ -235,7 +250,7 @@ bool chunks_valid(const Optim& o, std::string* why) {
             *why = "chunk " + std::to_string(i) + ": vector chunks must lead the table";
             return false;
         }
-        if (c.n == 0 || c.n > soarb::kChunkElems) {
+        if (c.n == 0 || c.n > o.chunk_elems) {
             *why = "chunk " + std::to_string(i) + ": bad length";
             return false;
         }
@@ -289,6 +304,12 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
     if (cudaError_t pe = soarb::prepare_kernels(); pe != cudaSuccess) {
         delete o;
         return fail(std::string("kernel set-up: ") + cudaGetErrorString(pe));
+    }
+    {
+        uint64_t total = 0;
+        for (const TensorRec& t : o->tensors)
+            if (t.grad) total += t.numel;
+        o->chunk_elems = choose_chunk_elems(total, sms * soarb::occupancy_apply(o->mixed));
     }
     build_chunks(*o);
     o->n_chunks = static_cast<int>(o->host_chunks.size());
@@ -407,6 +428,11 @@ soarb::ApplyArgs apply_args(const Optim& o, const double* parts, int n_parts) {
     a.parts = parts;
     a.bc = o.bc;
     a.bc_len = o.bc_len;
+    if (o.ema) {
+        a.ema_decay = o.ema_decay;
+        a.ema_omd = 1.0f - o.ema_decay;  // ema.hpp:24 evaluates (1.0f - decay_) in float
+        a.ema_delta = static_cast<long long>(o.ema - o.m);
+    }
     return a;
 }
 
@@ -417,7 +443,7 @@ int apply_impl(Optim& o, const double* parts, int n_parts, cudaStream_t s,
     if (rc != SOAR_OK) return rc;
     const soarb::ApplyArgs a = apply_args(o, parts, n_parts);
     SOAR_CUDA_TRY(soarb::launch_apply(o.mixed, o.chunks, o.n_chunks, o.n_vec, o.ctl, a,
-                                      o.grid_apply, s, ag));
+                                      o.grid_apply, s, ag, o.ema != nullptr));
     o.host_calls += 1;
     o.pending_coef = 1.0f;
     return SOAR_OK;
@@ -516,6 +542,7 @@ SOAR_API int soar_optim_destroy(void* handle) {
         cudaDeviceSynchronize();
         cudaFree(o->slab);
         if (o->bc) cudaFree(o->bc);
+        if (o->ema) cudaFree(o->ema);
     }
     delete o;
     return SOAR_OK;
@@ -661,6 +688,10 @@ SOAR_API int soar_optim_state_ptr(void* handle, int index, int kind, void** out_
         case SOAR_STATE_V:
             *out_ptr = o.v + t.state_off;
             return SOAR_OK;
+        case SOAR_STATE_EMA:
+            if (!o.ema) return fail("weight EMA is not enabled");
+            *out_ptr = o.ema + t.state_off;
+            return SOAR_OK;
         default:
             return fail("bad state kind");
     }
@@ -692,10 +723,195 @@ SOAR_API int soar_optim_write_state(void* handle, int index, int kind, const flo
     return SOAR_OK;
 }
 
+SOAR_API int soar_optim_enable_ema(void* handle, float decay, void* stream) {
+    if (!handle) return fail("null handle");
+    Optim& o = *as_optim(handle);
+    DeviceGuard g(o.device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (!o.ema) {
+        float* e = nullptr;
+        SOAR_CUDA_TRY(cudaMalloc(&e, std::max<uint64_t>(o.state_elems, 1) * sizeof(float)));
+        o.ema = e;
+    }
+    o.ema_decay = decay;
+    // ModelEMA::init_shadow (ema.hpp:52-58): the shadow starts as a copy of the weights
+    for (const TensorRec& t : o.tensors) {
+        if (!t.numel) continue;
+        const float* w = o.mixed ? o.master + t.state_off : static_cast<const float*>(t.param);
+        SOAR_CUDA_TRY(cudaMemcpyAsync(o.ema + t.state_off, w, t.numel * sizeof(float),
+                                      cudaMemcpyDeviceToDevice, s));
+    }
+    return SOAR_OK;
+}
+
+SOAR_API int soar_optim_ema_apply_to(void* handle, void* stream) {
+    if (!handle) return fail("null handle");
+    Optim& o = *as_optim(handle);
+    if (!o.ema) return fail("weight EMA is not enabled");
+    DeviceGuard g(o.device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // ModelEMA::apply_to (ema.hpp:31-38): the weights become the shadow
+    for (const TensorRec& t : o.tensors) {
+        if (!t.numel) continue;
+        if (o.mixed) {
+            SOAR_CUDA_TRY(cudaMemcpyAsync(o.master + t.state_off, o.ema + t.state_off,
+                                          t.numel * sizeof(float), cudaMemcpyDeviceToDevice, s));
+            SOAR_CUDA_TRY(soarb::launch_f32_to_bf16(o.ema + t.state_off,
+                                                    static_cast<uint16_t*>(t.param), t.numel, s));
+        } else {
+            SOAR_CUDA_TRY(cudaMemcpyAsync(t.param, o.ema + t.state_off, t.numel * sizeof(float),
+                                          cudaMemcpyDeviceToDevice, s));
+        }
+    }
+    return SOAR_OK;
+}
+
 SOAR_API int soar_optim_loss_scale_ptr(void* handle, float** out_ptr) {
     if (!handle || !out_ptr) return fail("null argument");
     *out_ptr = &as_optim(handle)->ctl->scale;
     return SOAR_OK;
+}
+
+// ---- optimizer-state checkpoint -------------------------------------------
+// The reference's weight-file record layout (src/nn/soar_model.cpp:427-463):
+// u32 magic 'SOAR', u32 version, u32 variant, u32 count, then per record
+// char name[128], u32 ndim, u32 shape[4], u64 bytes, raw bytes. Version 2
+// adds the optimizer's records; the reference's loader skips names it does not
+// know (soar_model.cpp:508-518), so a model-weights reader still works.
+
+namespace {
+constexpr uint32_t kSoarMagic = 0x534F4152u;
+constexpr uint32_t kStateVersion = 2;
+constexpr const char* kKindName[4] = {"master", "m", "v", "ema"};
+
+struct Counters {  // payload of the "optim.counters" record
+    uint64_t t, skipped, host_calls;
+    float scale;
+    int32_t tracker;
+    float lr;
+    uint32_t layout;
+    uint64_t n_tensors;
+};
+
+bool write_record(FILE* f, const std::string& name, uint64_t numel, const void* data,
+                  uint64_t bytes) {
+    char nb[128]{0};
+    std::strncpy(nb, name.c_str(), 127);
+    const uint32_t ndim = 1;
+    uint32_t shape[4] = {static_cast<uint32_t>(numel), 1, 1, 1};
+    return std::fwrite(nb, 128, 1, f) == 1 && std::fwrite(&ndim, 4, 1, f) == 1 &&
+           std::fwrite(shape, 16, 1, f) == 1 && std::fwrite(&bytes, 8, 1, f) == 1 &&
+           (bytes == 0 || std::fwrite(data, 1, bytes, f) == bytes);
+}
+}  // namespace
+
+SOAR_API int soar_optim_save_state(void* handle, const char* path) {
+    if (!handle || !path) return fail("null argument");
+    Optim& o = *as_optim(handle);
+    DeviceGuard g(o.device);
+    SOAR_CUDA_TRY(cudaDeviceSynchronize());
+    soarb::Ctl c{};
+    SOAR_CUDA_TRY(cudaMemcpy(&c, o.ctl, sizeof c, cudaMemcpyDeviceToHost));
+    FILE* f = std::fopen(path, "wb");
+    if (!f) return fail(std::string("cannot open ") + path);
+    const int kinds = o.ema ? 4 : 3;
+    const uint32_t n_records = 1 + kinds * static_cast<uint32_t>(o.tensors.size());
+    const uint32_t hdr[4] = {kSoarMagic, kStateVersion, 0u, n_records};
+    bool ok = std::fwrite(hdr, 4, 4, f) == 4;
+    Counters ct{c.t, c.skipped, o.host_calls, c.scale, c.tracker, o.lr,
+                static_cast<uint32_t>(o.opts.layout), o.tensors.size()};
+    ok = ok && write_record(f, "optim.counters", sizeof ct / 4, &ct, sizeof ct);
+    std::vector<float> buf;
+    for (size_t i = 0; ok && i < o.tensors.size(); ++i) {
+        const TensorRec& t = o.tensors[i];
+        buf.resize(t.numel);
+        for (int k = 0; ok && k < kinds; ++k) {
+            void* p = nullptr;
+            soar_optim_state_ptr(handle, static_cast<int>(i), k, &p);
+            if (t.numel && cudaMemcpy(buf.data(), p, t.numel * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+                ok = false;
+            ok = ok && write_record(f, std::string("optim.") + kKindName[k] + "." + std::to_string(i),
+                                    t.numel, buf.data(), t.numel * 4);
+        }
+    }
+    ok = (std::fclose(f) == 0) && ok;
+    return ok ? SOAR_OK : fail(std::string("writing ") + path + " failed");
+}
+
+SOAR_API int soar_optim_load_state(void* handle, const char* path, void* stream) {
+    if (!handle || !path) return fail("null argument");
+    Optim& o = *as_optim(handle);
+    DeviceGuard g(o.device);
+    FILE* f = std::fopen(path, "rb");
+    if (!f) return fail(std::string("cannot open ") + path);
+    uint32_t hdr[4]{};
+    if (std::fread(hdr, 4, 4, f) != 4 || hdr[0] != kSoarMagic) {
+        std::fclose(f);
+        return fail("not a SOAR file (bad magic)");
+    }
+    if (hdr[1] < kStateVersion) {
+        std::fclose(f);
+        return fail("weights-only file (version < 2): no optimizer state");
+    }
+    std::map<std::string, std::pair<int, int>> want;  // name -> (tensor, kind)
+    const int kinds = o.ema ? 4 : 3;
+    for (size_t i = 0; i < o.tensors.size(); ++i)
+        for (int k = 0; k < kinds; ++k)
+            want[std::string("optim.") + kKindName[k] + "." + std::to_string(i)] = {static_cast<int>(i), k};
+    bool have_counters = false;
+    Counters ct{};
+    size_t loaded = 0;
+    std::vector<float> buf;
+    SOAR_CUDA_TRY(cudaDeviceSynchronize());
+    for (uint32_t r = 0; r < hdr[3]; ++r) {
+        char nb[128]{0};
+        uint32_t ndim = 0, shape[4]{};
+        uint64_t bytes = 0;
+        if (std::fread(nb, 128, 1, f) != 1 || std::fread(&ndim, 4, 1, f) != 1 ||
+            std::fread(shape, 16, 1, f) != 1 || std::fread(&bytes, 8, 1, f) != 1)
+            break;
+        nb[127] = 0;
+        const std::string name(nb);
+        if (name == "optim.counters" && bytes == sizeof ct) {
+            have_counters = std::fread(&ct, sizeof ct, 1, f) == 1;
+            continue;
+        }
+        auto it = want.find(name);
+        if (it == want.end() || bytes != o.tensors[it->second.first].numel * 4) {
+            std::fseek(f, static_cast<long>(bytes), SEEK_CUR);  // skip, as the reference's loader
+            continue;
+        }
+        buf.resize(bytes / 4);
+        if (bytes && std::fread(buf.data(), 1, bytes, f) != bytes) break;
+        void* p = nullptr;
+        soar_optim_state_ptr(handle, it->second.first, it->second.second, &p);
+        if (bytes && cudaMemcpy(p, buf.data(), bytes, cudaMemcpyHostToDevice) != cudaSuccess) {
+            std::fclose(f);
+            return fail("state upload failed");
+        }
+        ++loaded;
+    }
+    std::fclose(f);
+    if (!have_counters) return fail("no optim.counters record");
+    if (ct.n_tensors != o.tensors.size() || ct.layout != static_cast<uint32_t>(o.opts.layout))
+        return fail("checkpoint was written by an optimizer with a different tensor list or layout");
+    if (loaded != static_cast<size_t>(kinds) * o.tensors.size())
+        return fail("checkpoint is missing optimizer records (" + std::to_string(loaded) + " of " +
+                    std::to_string(kinds * o.tensors.size()) + ")");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (o.mixed) {  // bf16 params follow the restored fp32 master
+        for (size_t i = 0; i < o.tensors.size(); ++i) {
+            const TensorRec& t = o.tensors[i];
+            SOAR_CUDA_TRY(soarb::launch_f32_to_bf16(o.master + t.state_off,
+                                                    static_cast<uint16_t*>(t.param), t.numel, s));
+        }
+    }
+    SOAR_CUDA_TRY(soarb::launch_set_counters(o.ctl, ct.t, ct.skipped, ct.scale, ct.tracker, s));
+    o.host_calls = std::max(ct.host_calls, ct.t + ct.skipped);
+    o.lr = ct.lr;
+    o.pending_coef = 1.0f;
+    SOAR_CUDA_TRY(cudaStreamSynchronize(s));
+    return ensure_bias_table(o);
 }
 
 SOAR_API int soar_cosine_create(void* optim_handle, uint64_t total_steps, float eta_min,

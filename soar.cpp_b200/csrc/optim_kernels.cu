@@ -185,7 +185,12 @@ __device__ __forceinline__ float prep_grad(float graw, const StepCoeffs& k) {
 
 // Elements [from, to) of a chunk, straight from global memory. With kAg the
 // updated params are also written into every peer's parameter buffer.
-template <bool kMixed, bool kAg>
+// ModelEMA::update (ema.hpp:24) for one weight: decay*shadow + (1-decay)*weight.
+__device__ __forceinline__ float ema_elem(float sh, float w, const ApplyArgs& a) {
+    return __fadd_rn(__fmul_rn(a.ema_decay, sh), __fmul_rn(a.ema_omd, w));
+}
+
+template <bool kMixed, bool kAg, bool kEma>
 __device__ __forceinline__ void apply_scalar(const Chunk& ch, uint32_t from, uint32_t to,
                                              uint32_t tid, uint32_t nthreads, const ApplyArgs& a,
                                              const StepCoeffs& k, float lr_wd, bool has_wd,
@@ -198,6 +203,10 @@ __device__ __forceinline__ void apply_scalar(const Chunk& ch, uint32_t from, uin
         ch.master[i] = th;
         ch.m[i] = m;
         ch.v[i] = v;
+        if constexpr (kEma) {
+            float* sh = ch.m + a.ema_delta;
+            sh[i] = ema_elem(sh[i], th, a);
+        }
         uint16_t pb = 0;
         if constexpr (kMixed) {
             pb = f32_to_bf16_rn(th);
@@ -230,11 +239,12 @@ __device__ __forceinline__ void for_each_tile(const Chunk* chunks, int n_vec, F&
     }
 }
 
-template <bool kMixed, bool kAg>
+template <bool kMixed, bool kAg, bool kEma>
 __global__ void __launch_bounds__(kApplyThreads, 1)
 k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restrict__ ctl,
         ApplyArgs a, AgArgs ag) {
     extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int kStages = apply_stages(kMixed, kEma);
     __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages];
     __shared__ StepCoeffs s_k;
     __shared__ int s_skip, s_found, s_err, s_drain_err;
@@ -247,9 +257,10 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
 
     constexpr uint32_t kGradBytes = kMixed ? 2u : 4u;
     constexpr uint32_t kVecElems = kVecBytes / kGradBytes;  // elements per 16 B of grad
-    constexpr uint32_t kStage = static_cast<uint32_t>(stage_bytes(kMixed));
+    constexpr uint32_t kStage = static_cast<uint32_t>(stage_bytes(kMixed, kEma));
     constexpr uint32_t kOffMaster = kGradBytes * kTile, kOffM = kOffMaster + 4u * kTile,
-                       kOffV = kOffM + 4u * kTile;
+                       kOffV = kOffM + 4u * kTile, kOffE = kOffV + 4u * kTile;
+    constexpr uint32_t kStreamBytes = kGradBytes + (kEma ? 16u : 12u);  // loaded per element
     constexpr int kConsumers = kConsumerWarps * 32;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -306,7 +317,7 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                         return false;
                     const uint32_t lv = len & ~(kVecElems - 1);
                     const uint32_t fb = smem_u32(&full_bar[s]);
-                    mbar_expect_tx(fb, (kGradBytes + 12u) * lv);
+                    mbar_expect_tx(fb, kStreamBytes * lv);
                     if (lv) {
                         const uint32_t base = smem_u32(smem + s * kStage);
                         bulk_load(base, static_cast<const char*>(ch.grad) + kGradBytes * t0,
@@ -314,6 +325,7 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                         bulk_load(base + kOffMaster, ch.master + t0, 4u * lv, fb);
                         bulk_load(base + kOffM, ch.m + t0, 4u * lv, fb);
                         bulk_load(base + kOffV, ch.v + t0, 4u * lv, fb);
+                        if constexpr (kEma) bulk_load(base + kOffE, ch.m + a.ema_delta + t0, 4u * lv, fb);
                     }
                     s_issued = q + 1;
                     return true;
@@ -335,6 +347,7 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                     float4* sms = reinterpret_cast<float4*>(st + kOffMaster);
                     float4* sm = reinterpret_cast<float4*>(st + kOffM);
                     float4* sv = reinterpret_cast<float4*>(st + kOffV);
+                    float4* se = reinterpret_cast<float4*>(st + kOffE);
                     const uint32_t nv = lv >> 2;
                     for (uint32_t i = tid; i < nv; i += kConsumers) {
                         float4 g;
@@ -353,6 +366,14 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                         sms[i] = th;
                         sm[i] = mm;
                         sv[i] = vv;
+                        if constexpr (kEma) {
+                            float4 e = se[i];
+                            e.x = ema_elem(e.x, th.x, a);
+                            e.y = ema_elem(e.y, th.y, a);
+                            e.z = ema_elem(e.z, th.z, a);
+                            e.w = ema_elem(e.w, th.w, a);
+                            se[i] = e;
+                        }
                         if constexpr (kMixed) {
                             // the bf16 params take the grad's place in the stage
                             uint2 p;
@@ -362,8 +383,8 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                         }
                     }
                     // the < 16-byte tail of the tile, straight from global memory
-                    apply_scalar<kMixed, kAg>(ch, t0 + lv, t0 + len, tid, kConsumers, a, k,
-                                              lr_wd, has_wd, ag);
+                    apply_scalar<kMixed, kAg, kEma>(ch, t0 + lv, t0 + len, tid, kConsumers, a,
+                                                    k, lr_wd, has_wd, ag);
                 }
                 // make the stage's generic-proxy writes visible to the bulk store;
                 // after the barrier every consumer reads the same failure flag
@@ -378,6 +399,7 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                         bulk_store(ch.master + t0, base + kOffMaster, 4u * lv);
                         bulk_store(ch.m + t0, base + kOffM, 4u * lv);
                         bulk_store(ch.v + t0, base + kOffV, 4u * lv);
+                        if constexpr (kEma) bulk_store(ch.m + a.ema_delta + t0, base + kOffE, 4u * lv);
                         if constexpr (kAg) {
                             // the fused all-gather: the same param tile into every peer
                             const size_t off = static_cast<const char*>(ch.param) -
@@ -399,8 +421,8 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
             // scalar chunks (misaligned heads, mixed-phase tensors)
             for (int c = s_err ? n_chunks : n_vec + static_cast<int>(blockIdx.x); c < n_chunks; c += gridDim.x) {
                 const Chunk ch = chunks[c];
-                apply_scalar<kMixed, kAg>(ch, 0, ch.n, tid, kConsumers, a, k,
-                                          __fmul_rn(a.lr, ch.wd), ch.wd != 0.0f, ag);
+                apply_scalar<kMixed, kAg, kEma>(ch, 0, ch.n, tid, kConsumers, a, k,
+                                                __fmul_rn(a.lr, ch.wd), ch.wd != 0.0f, ag);
             }
         }
     }
@@ -467,6 +489,13 @@ __global__ void k_bf16_to_f32(const uint16_t* __restrict__ src, float* __restric
         dst[i] = bf16_bits_to_f32(src[i]);
 }
 
+__global__ void k_f32_to_bf16(const float* __restrict__ src, uint16_t* __restrict__ dst,
+                              uint64_t n) {
+    for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+        dst[i] = f32_to_bf16_rn(src[i]);
+}
+
 __global__ void k_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float scale,
                                int32_t tracker) {
     ctl->t = t;
@@ -482,15 +511,19 @@ __global__ void k_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float sca
 
 cudaError_t prepare_kernels() {
     cudaError_t e = cudaSuccess;
-    auto set = [&](auto kern, bool mixed) {
+    auto set = [&](auto kern, bool mixed, bool ema) {
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(apply_smem_bytes(mixed)));
+                                     static_cast<int>(apply_smem_bytes(mixed, ema)));
     };
-    set(k_apply<true, false>, true);
-    set(k_apply<false, false>, false);
-    set(k_apply<true, true>, true);
-    set(k_apply<false, true>, false);
+    set(k_apply<true, false, false>, true, false);
+    set(k_apply<false, false, false>, false, false);
+    set(k_apply<true, true, false>, true, false);
+    set(k_apply<false, true, false>, false, false);
+    set(k_apply<true, false, true>, true, true);
+    set(k_apply<false, false, true>, false, true);
+    set(k_apply<true, true, true>, true, true);
+    set(k_apply<false, true, true>, false, true);
     return e;
 }
 
@@ -506,24 +539,28 @@ cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl*
     return cudaGetLastError();
 }
 
+template <bool kMixed, bool kAg, bool kEma>
+static void launch_apply_t(const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
+                           const ApplyArgs& args, int grid, cudaStream_t stream, const AgArgs& ag) {
+    k_apply<kMixed, kAg, kEma><<<grid, kApplyThreads, apply_smem_bytes(kMixed, kEma), stream>>>(
+        chunks, n_chunks, n_vec, ctl, args, ag);
+}
+
 cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
-                         const ApplyArgs& args, int grid, cudaStream_t stream, const AgArgs* ag) {
+                         const ApplyArgs& args, int grid, cudaStream_t stream, const AgArgs* ag,
+                         bool ema) {
     const AgArgs none{};
-    const size_t smem = apply_smem_bytes(mixed);
-    if (ag) {
-        if (mixed)
-            k_apply<true, true><<<grid, kApplyThreads, smem, stream>>>(chunks, n_chunks, n_vec,
-                                                                      ctl, args, *ag);
-        else
-            k_apply<false, true><<<grid, kApplyThreads, smem, stream>>>(chunks, n_chunks, n_vec,
-                                                                       ctl, args, *ag);
-    } else {
-        if (mixed)
-            k_apply<true, false><<<grid, kApplyThreads, smem, stream>>>(chunks, n_chunks, n_vec,
-                                                                       ctl, args, none);
-        else
-            k_apply<false, false><<<grid, kApplyThreads, smem, stream>>>(chunks, n_chunks, n_vec,
-                                                                        ctl, args, none);
+    const AgArgs& g = ag ? *ag : none;
+    const int sel = (mixed ? 4 : 0) | (ag ? 2 : 0) | (ema ? 1 : 0);
+    switch (sel) {
+        case 0: launch_apply_t<false, false, false>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
+        case 1: launch_apply_t<false, false, true>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
+        case 2: launch_apply_t<false, true, false>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
+        case 3: launch_apply_t<false, true, true>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
+        case 4: launch_apply_t<true, false, false>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
+        case 5: launch_apply_t<true, false, true>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
+        case 6: launch_apply_t<true, true, false>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
+        default: launch_apply_t<true, true, true>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
     }
     return cudaGetLastError();
 }
@@ -543,6 +580,15 @@ cudaError_t launch_bf16_to_f32(const uint16_t* src, float* dst, uint64_t n,
     return cudaGetLastError();
 }
 
+cudaError_t launch_f32_to_bf16(const float* src, uint16_t* dst, uint64_t n,
+                               cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    uint64_t blocks = (n + kThreads - 1) / kThreads;
+    if (blocks > 4096) blocks = 4096;
+    k_f32_to_bf16<<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(src, dst, n);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float scale,
                                 int32_t tracker, cudaStream_t stream) {
     k_set_counters<<<1, 1, 0, stream>>>(ctl, t, skipped, scale, tracker);
@@ -558,14 +604,20 @@ int occupancy_grad_sumsq(bool bf16) {
     return n > 0 ? n : 1;
 }
 
-int occupancy_apply(bool mixed) {
+int occupancy_apply(bool mixed, bool ema) {
     int n = 0;
-    if (mixed)
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<true, false>, kApplyThreads,
-                                                      apply_smem_bytes(true));
+    if (mixed && ema)
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<true, false, true>, kApplyThreads,
+                                                      apply_smem_bytes(true, true));
+    else if (mixed)
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<true, false, false>,
+                                                      kApplyThreads, apply_smem_bytes(true));
+    else if (ema)
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<false, false, true>,
+                                                      kApplyThreads, apply_smem_bytes(false, true));
     else
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<false, false>, kApplyThreads,
-                                                      apply_smem_bytes(false));
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<false, false, false>,
+                                                      kApplyThreads, apply_smem_bytes(false));
     return n > 0 ? n : 1;
 }
 

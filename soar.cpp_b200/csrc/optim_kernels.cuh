@@ -70,6 +70,9 @@ struct ApplyArgs {
     const double* parts;  // device, n_parts partial sums (rank order)
     const float2* bc;     // device table, bc[t] = (1 - beta1^t, sqrt(1 - beta2^t)), t >= 1
     uint32_t bc_len;      // entries in bc; t >= bc_len uses bc[bc_len - 1]
+    // fused weight EMA (ModelEMA::update): shadow = decay*shadow + (1-decay)*weight
+    float ema_decay, ema_omd; // decay and (1 - decay) rounded as the reference's float expression
+    long long ema_delta;      // element offset from a chunk's m pointer to its shadow pointer
 };
 
 // Data-parallel all-gather fused into the update: after a tile of the rank's
@@ -88,15 +91,21 @@ struct AgArgs {
 // Update-kernel pipeline shape (measured best on B200 for the mixed layout:
 // 1024-element tiles, 6 stages, 12 consumer warps + 1 producer warp, 2 CTAs/SM).
 constexpr int kTile = 1024;
-constexpr int kStages = 6;
+constexpr int kMaxStages = 6;
 constexpr int kConsumerWarps = 12;
 constexpr int kApplyThreads = (kConsumerWarps + 1) * 32;
-// bytes of one pipeline stage: grad tile + master, m, v tiles
-__host__ __device__ constexpr size_t stage_bytes(bool mixed) {
-    return (mixed ? 2u : 4u) * kTile + 12u * kTile;
+// bytes of one pipeline stage: grad tile + master, m, v (+ EMA shadow) tiles
+__host__ __device__ constexpr size_t stage_bytes(bool mixed, bool ema = false) {
+    return (mixed ? 2u : 4u) * kTile + (ema ? 16u : 12u) * kTile;
 }
-__host__ __device__ constexpr size_t apply_smem_bytes(bool mixed) {
-    return stage_bytes(mixed) * kStages;
+// stages that keep two CTAs per SM (<= ~108 KB of ring each)
+__host__ __device__ constexpr int apply_stages(bool mixed, bool ema = false) {
+    return static_cast<int>(110592 / stage_bytes(mixed, ema)) < kMaxStages
+               ? static_cast<int>(110592 / stage_bytes(mixed, ema))
+               : kMaxStages;
+}
+__host__ __device__ constexpr size_t apply_smem_bytes(bool mixed, bool ema = false) {
+    return stage_bytes(mixed, ema) * apply_stages(mixed, ema);
 }
 
 // Launchers (optim_kernels.cu). Each returns the launch status.
@@ -104,12 +113,15 @@ cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl*
                               double* partials, int grid, int use_scaler, double* out,
                               cudaStream_t stream);
 // ag == nullptr: plain update; otherwise the update with the fused all-gather.
+// ema: also update the weight EMA shadow (args.ema_*).
 cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
                          const ApplyArgs& args, int grid, cudaStream_t stream,
-                         const AgArgs* ag = nullptr);
+                         const AgArgs* ag = nullptr, bool ema = false);
 cudaError_t launch_scale_grads_f32(const Chunk* chunks, int n_chunks, float coef, int grid,
                                    cudaStream_t stream);
 cudaError_t launch_bf16_to_f32(const uint16_t* src, float* dst, uint64_t n,
+                               cudaStream_t stream);
+cudaError_t launch_f32_to_bf16(const float* src, uint16_t* dst, uint64_t n,
                                cudaStream_t stream);
 cudaError_t launch_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float scale,
                                 int32_t tracker, cudaStream_t stream);
@@ -119,7 +131,7 @@ cudaError_t prepare_kernels();
 
 // Resident CTAs per SM of each kernel at its launch configuration.
 int occupancy_grad_sumsq(bool bf16);
-int occupancy_apply(bool mixed);
+int occupancy_apply(bool mixed, bool ema = false);
 
 constexpr int kThreads = 256;
 

@@ -8,8 +8,8 @@ ctypes, plus the ZeRO-1 data-parallel driver (dp.py).
 """
 from .optim import (AdamW, AdamWOptions, CosineAnnealingLR, LossScalerOptions, ParamGroup,
                     SoarError, StepInfo, LAYOUT_FP32, LAYOUT_BF16_MIXED, STATE_MASTER,
-                    STATE_M, STATE_V, lib, library_path)
+                    STATE_M, STATE_V, STATE_EMA, lib, library_path)
 
 __all__ = ["AdamW", "AdamWOptions", "CosineAnnealingLR", "LossScalerOptions", "ParamGroup",
            "SoarError", "StepInfo", "LAYOUT_FP32", "LAYOUT_BF16_MIXED", "STATE_MASTER",
-           "STATE_M", "STATE_V", "lib", "library_path"]
+           "STATE_M", "STATE_V", "STATE_EMA", "lib", "library_path"]

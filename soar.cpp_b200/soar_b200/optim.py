@@ -24,7 +24,7 @@ from . import _build
 
 LAYOUT_FP32 = 0
 LAYOUT_BF16_MIXED = 1
-STATE_MASTER, STATE_M, STATE_V = 0, 1, 2
+STATE_MASTER, STATE_M, STATE_V, STATE_EMA = 0, 1, 2, 3
 
 
 class SoarError(RuntimeError):
@@ -78,6 +78,10 @@ SIGNATURES: dict[str, tuple] = {
     "soar_optim_read_state": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "soar_optim_write_state": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "soar_optim_loss_scale_ptr": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "soar_optim_enable_ema": (C.c_int, [C.c_void_p, C.c_float, C.c_void_p]),
+    "soar_optim_ema_apply_to": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "soar_optim_save_state": (C.c_int, [C.c_void_p, C.c_char_p]),
+    "soar_optim_load_state": (C.c_int, [C.c_void_p, C.c_char_p, C.c_void_p]),
     "soar_optim_grad_sumsq": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     "soar_optim_apply": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
     "soar_cosine_create": (C.c_int, [C.c_void_p, C.c_uint64, C.c_float, C.c_uint64,
@@ -320,6 +324,24 @@ class AdamW:
             raise ValueError("size mismatch")
         _check(lib().soar_optim_write_state(self.handle, index, kind, v.ctypes.data),
                "soar_optim_write_state")
+
+    def enable_ema(self, decay: float = 0.9999, stream=None) -> None:
+        """Weight EMA fused into the update (ModelEMA: shadow starts as the weights)."""
+        _check(lib().soar_optim_enable_ema(self.handle, decay, _stream_handle(stream)),
+               "soar_optim_enable_ema")
+
+    def ema_apply_to(self, stream=None) -> None:
+        _check(lib().soar_optim_ema_apply_to(self.handle, _stream_handle(stream)),
+               "soar_optim_ema_apply_to")
+
+    def save_state(self, path) -> None:
+        """Optimizer-state checkpoint (master/m/v + counters), SOAR v2 records."""
+        _check(lib().soar_optim_save_state(self.handle, str(path).encode()),
+               "soar_optim_save_state")
+
+    def load_state(self, path, stream=None) -> None:
+        _check(lib().soar_optim_load_state(self.handle, str(path).encode(),
+                                           _stream_handle(stream)), "soar_optim_load_state")
 
     def loss_scale_ptr(self) -> int:
         out = C.c_void_p()

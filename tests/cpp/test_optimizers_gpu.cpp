@@ -1,0 +1,131 @@
+// The reference's optimizer tests (tests/test_optimizers.cpp:12-49, :97-119)
+// run against the B200 C++ API (include/soar_optim.hpp) on the GPU, with the
+// reference's own parameter-list shape: std::vector<TensorPtr> where a tensor
+// exposes numel(), cuda_data() and grad() (tensor.hpp:47,80,95). Also checks
+// the Trainer's clip -> step -> zero_grad sequence (trainer.cpp:157-159), the
+// move the Trainer does (trainer.hpp:100) and the scheduler binding.
+// Exit code 0 = pass. No assert(): the checks stay on in release builds.
+#include <cmath>
+#include <cstdio>
+#include <memory>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+#include "soar_optim.hpp"
+
+namespace {
+
+int g_failures = 0;
+#define CHECK(cond, ...)                                      \
+    do {                                                      \
+        if (!(cond)) {                                        \
+            std::printf("FAIL %s:%d: ", __FILE__, __LINE__);  \
+            std::printf(__VA_ARGS__);                         \
+            std::printf("\n");                                \
+            ++g_failures;                                     \
+        }                                                     \
+    } while (0)
+
+// Minimal device tensor with the reference Tensor's optimizer-facing surface.
+class DevTensor;
+using TensorPtr = std::shared_ptr<DevTensor>;
+class DevTensor {
+public:
+    explicit DevTensor(std::vector<float> v) : n_(v.size()) {
+        cudaMalloc(&d_, n_ * sizeof(float));
+        cudaMemcpy(d_, v.data(), n_ * sizeof(float), cudaMemcpyHostToDevice);
+    }
+    ~DevTensor() { cudaFree(d_); }
+    size_t numel() const noexcept { return n_; }
+    float* cuda_data() noexcept { return d_; }
+    TensorPtr grad() const noexcept { return grad_; }
+    void set_grad(TensorPtr g) { grad_ = std::move(g); }
+    std::vector<float> host() const {
+        std::vector<float> v(n_);
+        cudaDeviceSynchronize();
+        cudaMemcpy(v.data(), d_, n_ * sizeof(float), cudaMemcpyDeviceToHost);
+        return v;
+    }
+
+private:
+    float* d_{nullptr};
+    size_t n_;
+    TensorPtr grad_;
+};
+
+TensorPtr make(std::vector<float> v) { return std::make_shared<DevTensor>(std::move(v)); }
+
+void test_adamw_parity() {
+    // tests/test_optimizers.cpp:12-49
+    auto p = make({1.0f});
+    p->set_grad(make({0.5f}));
+    soar::optim::AdamWOptions opt;
+    opt.lr = 1e-3f;
+    opt.beta1 = 0.9f;
+    opt.beta2 = 0.999f;
+    opt.eps = 1e-8f;
+    opt.weight_decay = 1e-2f;
+    soar::optim::AdamW optimizer(std::vector<TensorPtr>{p}, opt);
+    optimizer.step();
+    const float actual = p->host()[0];
+    std::printf("  AdamW step 1: actual = %.9g, expected = 0.99899\n", actual);
+    CHECK(std::fabs(actual - 0.99899f) < 1e-6f, "adamw parity %.9g", actual);
+}
+
+void test_gradient_clipping() {
+    // tests/test_optimizers.cpp:97-119
+    auto p = make({3.0f, 4.0f});
+    auto g = make({3.0f, 4.0f});
+    p->set_grad(g);
+    soar::optim::AdamW optimizer(std::vector<TensorPtr>{p});
+    const float norm = optimizer.clip_grad_norm(2.5f);
+    CHECK(std::fabs(norm - 5.0f) < 1e-5f, "norm %.9g", norm);
+    const auto gh = g->host();
+    const float nn = std::sqrt(gh[0] * gh[0] + gh[1] * gh[1]);
+    CHECK(std::fabs(nn - 2.5f) < 1e-5f, "clipped norm %.9g", nn);
+}
+
+void test_trainer_sequence_and_move() {
+    // clip -> step -> zero_grad (trainer.cpp:157-159) on an optimizer that was
+    // moved into its owner (trainer.hpp:100), with the scheduler bound first
+    // (main.cpp:712-716): the scheduler must still drive the moved optimizer.
+    auto p = make({1.0f, -2.0f, 0.5f});
+    auto p2 = make({0.25f});  // no grad: skipped (adamw.cpp:133-134)
+    p->set_grad(make({0.1f, 0.2f, -0.3f}));
+    soar::optim::AdamWOptions o;
+    o.lr = 1e-2f;
+    soar::optim::AdamW first(std::vector<TensorPtr>{p, p2}, o);
+    soar::optim::CosineAnnealingLR sched(first, 10, 1e-5f, 0);
+    soar::optim::AdamW owned(std::move(first));
+    const float n = owned.clip_grad_norm(2.0f);
+    owned.step();
+    owned.zero_grad();
+    sched.step();
+    CHECK(n > 0.37f && n < 0.38f, "norm %.9g", n);
+    CHECK(p->grad()->host()[1] == 0.0f, "zero_grad");
+    CHECK(p2->host()[0] == 0.25f, "param without grad changed");
+    CHECK(owned.get_lr() < 1e-2f, "scheduler did not reach the moved optimizer (lr %.9g)",
+          owned.get_lr());
+    CHECK(owned.info().step == 1, "step count");
+}
+
+}  // namespace
+
+int main() {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        std::printf("no CUDA device\n");
+        return 77;  // the reference's CTest skip code (CMakeLists.txt:196)
+    }
+    std::printf("=== SOAR optimizer tests on the B200 C++ API ===\n");
+    test_adamw_parity();
+    test_gradient_clipping();
+    test_trainer_sequence_and_move();
+    if (g_failures) {
+        std::printf("%d FAILURE(S)\n", g_failures);
+        return 1;
+    }
+    std::printf("ALL OPTIMIZER TESTS PASSED\n");
+    return 0;
+}

@@ -214,3 +214,33 @@ def test_reduce_avg_bf16(oracle_mod):
     f = sum(synth.from_bf16_bits(x).astype(np.float32) for x in ins)
     want = synth.to_bf16_bits((f * np.float32(0.25)).astype(np.float32))
     np.testing.assert_array_equal(out, want)
+
+
+def test_kat_model_ema_ref(ref_oracle):
+    """tests/test_metrics_preprocess.cpp:103-123: decay 0.9, a weight moved by
+    +10 -> shadow 0.9*orig + 0.1*(orig+10) within 1e-4; apply_to copies it."""
+    o = ref_oracle
+    p = synth.normal(synth.seed_of(70), 16, 0.02)
+    orig = float(p[0])
+    e = o.RefEma([p], 0.9)
+    p[0] = np.float32(orig + 10.0)
+    e.update()
+    expected = 0.9 * orig + 0.1 * (orig + 10.0)
+    assert abs(e.shadow(0)[0] - expected) < 1e-4
+    e.apply_to()
+    assert abs(p[0] - expected) < 1e-4
+
+
+def test_ema_port_matches_reference_bitexact(ref_oracle):
+    o = ref_oracle
+    ws = [synth.normal(synth.seed_of(71, i), n, 1.0) for i, n in enumerate([7, 1000, 4097])]
+    e = o.RefEma(ws, 0.999)
+    shadow = [w.copy() for w in ws]
+    for step in range(5):
+        for i, w in enumerate(ws):
+            w += synth.normal(synth.seed_of(72, i, step), w.size, 0.1)
+        e.update()
+        for sh, w in zip(shadow, ws):
+            o.port().oracle_ema_update(sh, w, w.size, 0.999)
+    for i, sh in enumerate(shadow):
+        np.testing.assert_array_equal(sh.view(np.uint32), e.shadow(i).view(np.uint32))
