@@ -125,6 +125,34 @@ SOAR_API int soar_optim_create_uniform(void* const* params, void* const* grads,
                                        const uint64_t* numel, int n_tensors,
                                        const soar_adamw_opts* opts, void** out_handle);
 
+/* SGD on the same device step: replaces soar::optim::SGD
+   (include/soar/optim/sgd.hpp:9-38, src/optim/sgd.cpp). The first five fields
+   are the reference's SGDOptions (same defaults); the rest are the AdamW
+   extensions. The handle works with every soar_optim_* call (step, zero_grad,
+   clip_grad_norm, set/get_lr, info, state: MASTER and M = momentum buffer,
+   checkpoint, EMA, destroy). */
+typedef struct soar_sgd_opts {
+    float lr;               /* 1e-2 */
+    float momentum;         /* 0 */
+    float dampening;        /* 0 */
+    float weight_decay;     /* 0 (coupled: d_p += wd * theta, sgd.cpp:71-73) */
+    int32_t nesterov;       /* 0 */
+    int32_t layout;
+    float max_grad_norm;
+    int32_t use_loss_scaler;
+    float init_scale;
+    float growth_factor;
+    float backoff_factor;
+    int32_t growth_interval;
+    int32_t device;
+} soar_sgd_opts;
+
+SOAR_API void soar_sgd_default_opts(soar_sgd_opts* out);
+/* Replaces SGD::SGD(std::vector<TensorPtr>, SGDOptions) (sgd.cpp:6-16). Each
+   tensor's weight_decay is its own (parameter groups). */
+SOAR_API int soar_sgd_create(const soar_tensor_desc* tensors, int n_tensors,
+                             const soar_sgd_opts* opts, void** out_handle);
+
 SOAR_API int soar_optim_destroy(void* handle);
 
 /* Replaces AdamW::step() (adamw.cpp:119-176) -- and, with max_grad_norm > 0,

@@ -144,6 +144,87 @@ private:
     void* h_{nullptr};
 };
 
+struct SGDOptions {  // include/soar/optim/sgd.hpp:9-15, same fields and defaults
+    float lr{1e-2f};
+    float momentum{0.0f};
+    float dampening{0.0f};
+    float weight_decay{0.0f};
+    bool nesterov{false};
+};
+
+// soar::optim::SGD (sgd.hpp:21-38) on the same device step. Same methods as
+// the reference's (step, zero_grad, clip_grad_norm, set_lr, get_lr).
+class SGD {
+public:
+    template <class P>
+    explicit SGD(const std::vector<P>& params, SGDOptions options = {},
+                 AdamWExtOptions ext = {}) {
+        std::vector<soar_tensor_desc> d;
+        d.reserve(params.size());
+        for (const auto& p : params) {
+            soar_tensor_desc t{};
+            if (p) {
+                t.param = p->cuda_data();
+                auto g = p->grad();
+                t.grad = g ? g->cuda_data() : nullptr;
+                t.numel = static_cast<uint64_t>(p->numel());
+            }
+            t.weight_decay = options.weight_decay;
+            d.push_back(t);
+        }
+        soar_sgd_opts c;
+        soar_sgd_default_opts(&c);
+        c.lr = options.lr;
+        c.momentum = options.momentum;
+        c.dampening = options.dampening;
+        c.weight_decay = options.weight_decay;
+        c.nesterov = options.nesterov ? 1 : 0;
+        c.layout = ext.layout;
+        c.max_grad_norm = ext.max_grad_norm;
+        c.use_loss_scaler = ext.use_loss_scaler ? 1 : 0;
+        c.init_scale = ext.init_scale;
+        c.growth_factor = ext.growth_factor;
+        c.backoff_factor = ext.backoff_factor;
+        c.growth_interval = ext.growth_interval;
+        c.device = ext.device;
+        detail::check(soar_sgd_create(d.data(), static_cast<int>(d.size()), &c, &h_),
+                      "sgd_create");
+    }
+    SGD(SGD&& o) noexcept : h_(std::exchange(o.h_, nullptr)) {}
+    SGD& operator=(SGD&& o) noexcept {
+        if (this != &o) {
+            if (h_) soar_optim_destroy(h_);
+            h_ = std::exchange(o.h_, nullptr);
+        }
+        return *this;
+    }
+    SGD(const SGD&) = delete;
+    SGD& operator=(const SGD&) = delete;
+    ~SGD() {
+        if (h_) soar_optim_destroy(h_);
+    }
+
+    void step(void* stream = nullptr) { detail::check(soar_optim_step(h_, stream), "step"); }
+    void zero_grad(void* stream = nullptr) {
+        detail::check(soar_optim_zero_grad(h_, stream), "zero_grad");
+    }
+    float clip_grad_norm(float max_norm, void* stream = nullptr) {
+        float n = 0.0f;
+        detail::check(soar_optim_clip_grad_norm(h_, max_norm, &n, stream), "clip_grad_norm");
+        return n;
+    }
+    void set_lr(float lr) noexcept { soar_optim_set_lr(h_, lr); }
+    [[nodiscard]] float get_lr() const noexcept {
+        float lr = 0.0f;
+        soar_optim_get_lr(h_, &lr);
+        return lr;
+    }
+    [[nodiscard]] void* handle() const noexcept { return h_; }
+
+private:
+    void* h_{nullptr};
+};
+
 // CosineAnnealingLR(AdamW&, total_steps, eta_min = 1e-6f, warmup_steps = 0)
 // (adamw.hpp:45-57). Bound to the optimizer's handle, so it follows the
 // optimizer across moves (the reference binds a reference to the object).

@@ -263,6 +263,74 @@ int oracle_step(int layout, int n_tensors, void** params, void** grads, float** 
                                    backoff_factor, growth_interval, sumsq, st, scratch);
 }
 
+/* ---- SGD (reference src/optim/sgd.cpp:52-98) ---------------------------- */
+
+/* One tensor's SGD::step body (sgd.cpp:68-86); has_buf: the momentum buffer
+ * holds a previous step (has_momentum_buffer_, sgd.cpp:89). */
+void oracle_sgd_update_f32(float* theta, const float* grad, float* buf, size_t n, float lr,
+                           float momentum, float dampening, float weight_decay, int nesterov,
+                           int has_buf) {
+    for (size_t i = 0; i < n; ++i) {
+        float d_p = grad[i];
+        if (weight_decay != 0.0f) {
+            d_p += weight_decay * theta[i];
+        }
+        if (momentum != 0.0f) {
+            if (!has_buf) {
+                buf[i] = d_p;
+            } else {
+                buf[i] = momentum * buf[i] + (1.0f - dampening) * d_p;
+            }
+            if (nesterov) {
+                d_p = d_p + momentum * buf[i];
+            } else {
+                d_p = buf[i];
+            }
+        }
+        theta[i] -= lr * d_p;
+    }
+}
+
+/* The SGD step as the fused device step defines it (unscale, inf skip, clip,
+ * per-tensor wd, fp32 master, bf16 write-back, scaler), given the global sum
+ * of squares. buf[k]: momentum buffers. Returns 1 when skipped. */
+int oracle_sgd_apply_with_sumsq(int layout, int n_tensors, void** params, void** grads,
+                                float** master, float** buf, const uint64_t* numel,
+                                const float* wd, float lr, float momentum, float dampening,
+                                int nesterov, float max_norm, int use_scaler, float growth_factor,
+                                float backoff_factor, int32_t growth_interval, double sumsq,
+                                oracle_step_state* st, float* scratch) {
+    float inv_scale = use_scaler ? 1.0f / st->scale : 1.0f;
+    int found_inf = !isfinite(sumsq);
+    float norm = oracle_norm_from_sumsq(sumsq);
+    st->last_norm = norm;
+    st->last_found_inf = found_inf;
+    if (use_scaler && found_inf) {
+        st->skipped += 1;
+        st->last_clip_coef = 1.0f;
+        oracle_scaler_update(st, 1, growth_factor, backoff_factor, growth_interval);
+        return 1;
+    }
+    int clipped = 0;
+    float coef = max_norm > 0.0f ? oracle_clip_coef(norm, max_norm, &clipped) : 1.0f;
+    st->last_clip_coef = coef;
+    int has_buf = st->t > 0;
+    st->t += 1;
+    for (int k = 0; k < n_tensors; ++k) {
+        if (!grads[k] || numel[k] == 0) continue;
+        size_t n = numel[k];
+        if (layout == 1) oracle_unscale_bf16((const uint16_t*)grads[k], n, inv_scale, scratch);
+        else oracle_unscale_f32((const float*)grads[k], n, inv_scale, scratch);
+        if (clipped) oracle_scale_f32(scratch, n, coef);
+        float* theta = layout == 1 ? master[k] : (float*)params[k];
+        oracle_sgd_update_f32(theta, scratch, buf[k], n, lr, momentum, dampening, wd[k], nesterov,
+                              has_buf);
+        if (layout == 1) oracle_f32_to_bf16_array(theta, (uint16_t*)params[k], n);
+    }
+    if (use_scaler) oracle_scaler_update(st, 0, growth_factor, backoff_factor, growth_interval);
+    return 0;
+}
+
 /* ModelEMA::update (reference include/soar/utils/ema.hpp:18-28) over one
  * weight array: shadow = decay * shadow + (1 - decay) * weight. */
 void oracle_ema_update(float* shadow, const float* weight, size_t n, float decay) {

@@ -98,6 +98,12 @@ def _load_port() -> C.CDLL:
                                 C.c_int32, C.POINTER(StepState), _f32p]
     lib.oracle_reduce_avg_bf16.argtypes = [C.c_int, C.POINTER(C.c_void_p), C.c_size_t, _u16p]
     lib.oracle_ema_update.argtypes = [_f32p, _f32p, C.c_size_t, C.c_float]
+    lib.oracle_sgd_apply_with_sumsq.restype = C.c_int
+    lib.oracle_sgd_apply_with_sumsq.argtypes = [
+        C.c_int, C.c_int, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+        C.POINTER(C.c_void_p), C.POINTER(C.c_uint64), C.POINTER(C.c_float), C.c_float, C.c_float,
+        C.c_float, C.c_int, C.c_float, C.c_int, C.c_float, C.c_float, C.c_int32, C.c_double,
+        C.POINTER(StepState), _f32p]
     lib.oracle_grad_sumsq.restype = C.c_double
     lib.oracle_grad_sumsq.argtypes = [C.c_int, C.c_int, C.POINTER(C.c_void_p),
                                       C.POINTER(C.c_uint64), C.c_float, C.POINTER(C.c_int), _f32p]
@@ -215,6 +221,32 @@ class PortOptimizer:
                     port().oracle_ema_update(self.ema[i], np.ascontiguousarray(self.weights(i)),
                                              self.numel[i], self.ema_decay)
         return skipped
+
+
+class PortSGD(PortOptimizer):
+    """Port oracle of the fused SGD step (oracle_sgd_apply_with_sumsq); the
+    momentum buffers live in self.m."""
+
+    def __init__(self, params, wd, cfg: StepConfig, momentum=0.0, dampening=0.0, nesterov=False,
+                 init_scale: float = 1.0):
+        super().__init__(params, wd, cfg, init_scale)
+        self.momentum, self.dampening, self.nesterov = momentum, dampening, nesterov
+
+    def step(self, grads, lr: float | None = None) -> int:
+        c = self.cfg
+        n = len(self.params)
+        grads = [None if g is None else np.ascontiguousarray(g) for g in grads]
+        numel = (C.c_uint64 * n)(*self.numel)
+        inv = (np.float32(1.0) / np.float32(self.state.scale)) if c.use_scaler else np.float32(1.0)
+        found = C.c_int()
+        sumsq = port().oracle_grad_sumsq(c.layout, n, _ptrs(grads), numel, float(inv),
+                                         C.byref(found), self.scratch)
+        return port().oracle_sgd_apply_with_sumsq(
+            c.layout, n, _ptrs(self.params), _ptrs(grads), _ptrs(self.master), _ptrs(self.m),
+            numel, (C.c_float * n)(*self.wd.tolist()), c.lr if lr is None else lr,
+            self.momentum, self.dampening, int(self.nesterov), c.max_norm, int(c.use_scaler),
+            c.growth_factor, c.backoff_factor, c.growth_interval, sumsq, C.byref(self.state),
+            self.scratch)
 
 
 class PortShard(PortOptimizer):
@@ -353,6 +385,41 @@ class RefAdamW:
     def set_moment(self, idx: int, which: int, val: np.ndarray):
         assert ref().soar_ref_adamw_set_moment(self.h, idx, which,
                                                np.ascontiguousarray(val, np.float32)) == 0
+
+
+class RefSGD:
+    """The reference's soar::optim::SGD over numpy fp32 buffers (in place)."""
+
+    def __init__(self, params, grads, lr=1e-2, momentum=0.0, dampening=0.0, weight_decay=0.0,
+                 nesterov=False):
+        lib = ref()
+        if not hasattr(lib, "_sgd_bound"):
+            lib.soar_ref_sgd_create.restype = C.c_void_p
+            lib.soar_ref_sgd_create.argtypes = [C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+                                                C.POINTER(C.c_uint64), C.c_int, C.c_float,
+                                                C.c_float, C.c_float, C.c_float, C.c_int]
+            lib.soar_ref_sgd_step.argtypes = [C.c_void_p]
+            lib.soar_ref_sgd_destroy.argtypes = [C.c_void_p]
+            lib.soar_ref_sgd_set_lr.argtypes = [C.c_void_p, C.c_float]
+            lib.soar_ref_sgd_clip_grad_norm.restype = C.c_float
+            lib.soar_ref_sgd_clip_grad_norm.argtypes = [C.c_void_p, C.c_float]
+            lib._sgd_bound = True
+        self.params, self.grads = params, grads
+        n = len(params)
+        self.h = lib.soar_ref_sgd_create(_ptrs(params), _ptrs(grads),
+                                         (C.c_uint64 * n)(*[p.size for p in params]), n, lr,
+                                         momentum, dampening, weight_decay, int(nesterov))
+
+    def step(self):
+        ref().soar_ref_sgd_step(self.h)
+
+    def clip_grad_norm(self, max_norm):
+        return ref().soar_ref_sgd_clip_grad_norm(self.h, max_norm)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            ref().soar_ref_sgd_destroy(self.h)
+            self.h = None
 
 
 class RefEma:

@@ -23,6 +23,7 @@
 #define private public
 #include <soar/optim/adamw.hpp>  // the reference header, unmodified
 #undef private
+#include <soar/optim/sgd.hpp>    // the reference header, unmodified
 #include <soar/nn/module.hpp>    // the stand-in (oracle/standin)
 #include <soar/utils/ema.hpp>    // the reference header, unmodified
 
@@ -31,6 +32,11 @@ namespace {
 struct RefOptim {
     std::vector<soar::TensorPtr> params;
     std::unique_ptr<soar::optim::AdamW> opt;
+};
+
+struct RefSgd {
+    std::vector<soar::TensorPtr> params;
+    std::unique_ptr<soar::optim::SGD> opt;
 };
 
 struct RefEma {
@@ -114,6 +120,32 @@ void* soar_ref_cosine_create(void* h, uint64_t total_steps, float eta_min, uint6
 void soar_ref_cosine_step(void* s) { static_cast<RefSched*>(s)->sched->step(); }
 
 void soar_ref_cosine_destroy(void* s) { delete static_cast<RefSched*>(s); }
+
+// The reference's SGD (src/optim/sgd.cpp) over numpy fp32 buffers.
+void* soar_ref_sgd_create(float** params, float** grads, const uint64_t* numel, int n, float lr,
+                          float momentum, float dampening, float wd, int nesterov) {
+    auto* h = new RefSgd();
+    for (int i = 0; i < n; ++i) {
+        auto p = std::make_shared<soar::Tensor>(params[i], static_cast<size_t>(numel[i]));
+        if (grads && grads[i])
+            p->set_grad(std::make_shared<soar::Tensor>(grads[i], static_cast<size_t>(numel[i])));
+        h->params.push_back(p);
+    }
+    soar::optim::SGDOptions o;
+    o.lr = lr;
+    o.momentum = momentum;
+    o.dampening = dampening;
+    o.weight_decay = wd;
+    o.nesterov = nesterov != 0;
+    h->opt = std::make_unique<soar::optim::SGD>(h->params, o);
+    return h;
+}
+void soar_ref_sgd_step(void* h) { static_cast<RefSgd*>(h)->opt->step(); }
+float soar_ref_sgd_clip_grad_norm(void* h, float max_norm) {
+    return static_cast<RefSgd*>(h)->opt->clip_grad_norm(max_norm);
+}
+void soar_ref_sgd_set_lr(void* h, float lr) { static_cast<RefSgd*>(h)->opt->set_lr(lr); }
+void soar_ref_sgd_destroy(void* h) { delete static_cast<RefSgd*>(h); }
 
 // The reference's ModelEMA over numpy weight buffers (viewed in place).
 void* soar_ref_ema_create(float** params, const uint64_t* numel, int n, float decay) {

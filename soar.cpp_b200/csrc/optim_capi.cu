@@ -65,6 +65,9 @@ struct TensorRec {
 struct Optim {
     int device = 0;
     bool mixed = false;
+    bool sgd = false;            // SGD (momentum buffer in m) instead of AdamW
+    float momentum = 0.0f, dampening = 0.0f;
+    bool nesterov = false;
     soar_adamw_opts opts{};
     float lr = 1e-3f;
     float pending_coef = 1.0f;   // from a standalone clip_grad_norm (mixed layout)
@@ -262,8 +265,13 @@ bool chunks_valid(const Optim& o, std::string* why) {
     return true;
 }
 
+struct SgdParams {
+    float momentum, dampening;
+    bool nesterov;
+};
+
 int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* opts,
-                void** out) {
+                void** out, const SgdParams* sgd = nullptr) {
     if (!opts || !out || n < 0 || (n > 0 && !tensors)) return fail("null argument");
     *out = nullptr;
     if (opts->layout != SOAR_LAYOUT_FP32 && opts->layout != SOAR_LAYOUT_BF16_MIXED)
@@ -273,6 +281,12 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
 
     auto* o = new Optim();
     o->opts = *opts;
+    if (sgd) {
+        o->sgd = true;
+        o->momentum = sgd->momentum;
+        o->dampening = sgd->dampening;
+        o->nesterov = sgd->nesterov;
+    }
     o->device = opts->device;
     o->mixed = opts->layout == SOAR_LAYOUT_BF16_MIXED;
     o->lr = opts->lr;
@@ -309,13 +323,14 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
         uint64_t total = 0;
         for (const TensorRec& t : o->tensors)
             if (t.grad) total += t.numel;
-        o->chunk_elems = choose_chunk_elems(total, sms * soarb::occupancy_apply(o->mixed));
+        o->chunk_elems =
+            choose_chunk_elems(total, sms * soarb::occupancy_apply(o->mixed, false, o->sgd));
     }
     build_chunks(*o);
     o->n_chunks = static_cast<int>(o->host_chunks.size());
     const int cap = std::max(1, o->n_chunks);
     o->grid_sumsq = std::min(sms * soarb::occupancy_grad_sumsq(o->mixed), cap);
-    o->grid_apply = std::min(sms * soarb::occupancy_apply(o->mixed), cap);
+    o->grid_apply = std::min(sms * soarb::occupancy_apply(o->mixed, false, o->sgd), cap);
 
     // Slab: [master | m | v | chunks | partials | ctl | clip scratch]
     const size_t state_bytes = o->state_elems * sizeof(float);
@@ -325,7 +340,7 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
     const size_t off_m = off;
     off = align_up(off + state_bytes, kSlabAlign);
     const size_t off_v = off;
-    off = align_up(off + state_bytes, kSlabAlign);
+    if (!o->sgd) off = align_up(off + state_bytes, kSlabAlign);  // SGD has no second moment
     const size_t off_chunks = off;
     off = align_up(off + o->host_chunks.size() * sizeof(soarb::Chunk), kSlabAlign);
     const size_t off_partials = off;
@@ -343,7 +358,7 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
     }
     o->master = o->mixed ? reinterpret_cast<float*>(o->slab + off_master) : nullptr;
     o->m = reinterpret_cast<float*>(o->slab + off_m);
-    o->v = reinterpret_cast<float*>(o->slab + off_v);
+    o->v = o->sgd ? nullptr : reinterpret_cast<float*>(o->slab + off_v);
     o->chunks = reinterpret_cast<soarb::Chunk*>(o->slab + off_chunks);
     o->partials = reinterpret_cast<double*>(o->slab + off_partials);
     o->ctl = reinterpret_cast<soarb::Ctl*>(o->slab + off_ctl);
@@ -353,7 +368,7 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
         const uint64_t s = static_cast<uint64_t>(reinterpret_cast<uintptr_t>(c.master));
         c.master = o->mixed ? o->master + s : static_cast<float*>(c.param);
         c.m = o->m + s;
-        c.v = o->v + s;
+        c.v = o->sgd ? nullptr : o->v + s;
     }
 
     auto cleanup = [&](const std::string& msg) {
@@ -371,7 +386,7 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
         cudaSuccess)
         return cleanup(std::string("chunk table upload: ") + cudaGetErrorString(e));
     if ((e = cudaMemset(o->m, 0, state_bytes)) != cudaSuccess ||
-        (e = cudaMemset(o->v, 0, state_bytes)) != cudaSuccess)
+        (o->v && (e = cudaMemset(o->v, 0, state_bytes)) != cudaSuccess))
         return cleanup(std::string("state zero-fill: ") + cudaGetErrorString(e));
     soarb::Ctl ctl{};
     ctl.scale = opts->use_loss_scaler ? opts->init_scale : 1.0f;
@@ -428,6 +443,11 @@ soarb::ApplyArgs apply_args(const Optim& o, const double* parts, int n_parts) {
     a.parts = parts;
     a.bc = o.bc;
     a.bc_len = o.bc_len;
+    if (o.sgd) {
+        a.momentum = o.momentum;
+        a.omdamp = 1.0f - o.dampening;  // sgd.cpp:80 evaluates (1.0f - dampening) in float
+        a.nesterov = o.nesterov ? 1 : 0;
+    }
     if (o.ema) {
         a.ema_decay = o.ema_decay;
         a.ema_omd = 1.0f - o.ema_decay;  // ema.hpp:24 evaluates (1.0f - decay_) in float
@@ -443,7 +463,7 @@ int apply_impl(Optim& o, const double* parts, int n_parts, cudaStream_t s,
     if (rc != SOAR_OK) return rc;
     const soarb::ApplyArgs a = apply_args(o, parts, n_parts);
     SOAR_CUDA_TRY(soarb::launch_apply(o.mixed, o.chunks, o.n_chunks, o.n_vec, o.ctl, a,
-                                      o.grid_apply, s, ag, o.ema != nullptr));
+                                      o.grid_apply, s, ag, o.ema != nullptr, o.sgd));
     o.host_calls += 1;
     o.pending_coef = 1.0f;
     return SOAR_OK;
@@ -531,6 +551,42 @@ SOAR_API int soar_optim_create_uniform(void* const* params, void* const* grads,
         return create_impl(d.data(), n_tensors, opts, out_handle);
     } catch (...) {
         return fail("exception in create_uniform");
+    }
+}
+
+SOAR_API void soar_sgd_default_opts(soar_sgd_opts* out) {
+    if (!out) return;
+    std::memset(out, 0, sizeof *out);
+    out->lr = 1e-2f;  // SGDOptions defaults, sgd.hpp:9-15
+    out->layout = SOAR_LAYOUT_FP32;
+    out->init_scale = 65536.0f;
+    out->growth_factor = 2.0f;
+    out->backoff_factor = 0.5f;
+    out->growth_interval = 200;
+}
+
+SOAR_API int soar_sgd_create(const soar_tensor_desc* tensors, int n_tensors,
+                             const soar_sgd_opts* opts, void** out_handle) {
+    if (!opts) return fail("null argument");
+    try {
+        soar_adamw_opts a;
+        soar_adamw_default_opts(&a);
+        a.lr = opts->lr;
+        a.weight_decay = opts->weight_decay;
+        a.layout = opts->layout;
+        a.max_grad_norm = opts->max_grad_norm;
+        a.use_loss_scaler = opts->use_loss_scaler;
+        a.init_scale = opts->init_scale;
+        a.growth_factor = opts->growth_factor;
+        a.backoff_factor = opts->backoff_factor;
+        a.growth_interval = opts->growth_interval;
+        a.device = opts->device;
+        const SgdParams sp{opts->momentum, opts->dampening, opts->nesterov != 0};
+        return create_impl(tensors, n_tensors, &a, out_handle, &sp);
+    } catch (const std::exception& ex) {
+        return fail(ex.what());
+    } catch (...) {
+        return fail("unknown exception");
     }
 }
 
@@ -686,6 +742,7 @@ SOAR_API int soar_optim_state_ptr(void* handle, int index, int kind, void** out_
             *out_ptr = o.m + t.state_off;
             return SOAR_OK;
         case SOAR_STATE_V:
+            if (!o.v) return fail("SGD has no second-moment state");
             *out_ptr = o.v + t.state_off;
             return SOAR_OK;
         case SOAR_STATE_EMA:
@@ -814,18 +871,21 @@ SOAR_API int soar_optim_save_state(void* handle, const char* path) {
     SOAR_CUDA_TRY(cudaMemcpy(&c, o.ctl, sizeof c, cudaMemcpyDeviceToHost));
     FILE* f = std::fopen(path, "wb");
     if (!f) return fail(std::string("cannot open ") + path);
-    const int kinds = o.ema ? 4 : 3;
-    const uint32_t n_records = 1 + kinds * static_cast<uint32_t>(o.tensors.size());
+    std::vector<int> kinds = {SOAR_STATE_MASTER, SOAR_STATE_M};
+    if (!o.sgd) kinds.push_back(SOAR_STATE_V);
+    if (o.ema) kinds.push_back(SOAR_STATE_EMA);
+    const uint32_t n_records = 1 + static_cast<uint32_t>(kinds.size() * o.tensors.size());
     const uint32_t hdr[4] = {kSoarMagic, kStateVersion, 0u, n_records};
     bool ok = std::fwrite(hdr, 4, 4, f) == 4;
     Counters ct{c.t, c.skipped, o.host_calls, c.scale, c.tracker, o.lr,
-                static_cast<uint32_t>(o.opts.layout), o.tensors.size()};
+                static_cast<uint32_t>(o.opts.layout) | (o.sgd ? 0x100u : 0u), o.tensors.size()};
     ok = ok && write_record(f, "optim.counters", sizeof ct / 4, &ct, sizeof ct);
     std::vector<float> buf;
     for (size_t i = 0; ok && i < o.tensors.size(); ++i) {
         const TensorRec& t = o.tensors[i];
         buf.resize(t.numel);
-        for (int k = 0; ok && k < kinds; ++k) {
+        for (int k : kinds) {
+            if (!ok) break;
             void* p = nullptr;
             soar_optim_state_ptr(handle, static_cast<int>(i), k, &p);
             if (t.numel && cudaMemcpy(buf.data(), p, t.numel * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
@@ -854,9 +914,11 @@ SOAR_API int soar_optim_load_state(void* handle, const char* path, void* stream)
         return fail("weights-only file (version < 2): no optimizer state");
     }
     std::map<std::string, std::pair<int, int>> want;  // name -> (tensor, kind)
-    const int kinds = o.ema ? 4 : 3;
+    std::vector<int> kinds = {SOAR_STATE_MASTER, SOAR_STATE_M};
+    if (!o.sgd) kinds.push_back(SOAR_STATE_V);
+    if (o.ema) kinds.push_back(SOAR_STATE_EMA);
     for (size_t i = 0; i < o.tensors.size(); ++i)
-        for (int k = 0; k < kinds; ++k)
+        for (int k : kinds)
             want[std::string("optim.") + kKindName[k] + "." + std::to_string(i)] = {static_cast<int>(i), k};
     bool have_counters = false;
     Counters ct{};
@@ -893,11 +955,12 @@ SOAR_API int soar_optim_load_state(void* handle, const char* path, void* stream)
     }
     std::fclose(f);
     if (!have_counters) return fail("no optim.counters record");
-    if (ct.n_tensors != o.tensors.size() || ct.layout != static_cast<uint32_t>(o.opts.layout))
+    if (ct.n_tensors != o.tensors.size() ||
+        ct.layout != (static_cast<uint32_t>(o.opts.layout) | (o.sgd ? 0x100u : 0u)))
         return fail("checkpoint was written by an optimizer with a different tensor list or layout");
-    if (loaded != static_cast<size_t>(kinds) * o.tensors.size())
+    if (loaded != kinds.size() * o.tensors.size())
         return fail("checkpoint is missing optimizer records (" + std::to_string(loaded) + " of " +
-                    std::to_string(kinds * o.tensors.size()) + ")");
+                    std::to_string(kinds.size() * o.tensors.size()) + ")");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (o.mixed) {  // bf16 params follow the restored fp32 master
         for (size_t i = 0; i < o.tensors.size(); ++i) {

@@ -163,9 +163,24 @@ k_grad_sumsq(const Chunk* __restrict__ chunks, int n_chunks, Ctl* __restrict__ c
 struct StepCoeffs {
     float inv;        // 1 / loss scale
     float coef;       // clip coefficient (1: no clip)
-    float step_size;  // lr / bias_correction1
-    float sqrt_bc2;
+    float step_size;  // lr / bias_correction1 (AdamW)
+    float sqrt_bc2;   // (AdamW)
+    int has_buf;      // SGD: momentum buffers hold a previous step (sgd.cpp:74-80)
 };
+
+// One element of SGD::step (reference src/optim/sgd.cpp:68-86): coupled weight
+// decay, momentum with dampening, optional Nesterov, theta -= lr * d_p. `m`
+// is the momentum buffer.
+__device__ __forceinline__ void sgd_elem(float& th, float& m, float g, const ApplyArgs& a,
+                                         const StepCoeffs& k, float wd) {
+    float d = g;
+    if (wd != 0.0f) d = __fadd_rn(d, __fmul_rn(wd, th));
+    if (a.momentum != 0.0f) {
+        m = k.has_buf ? __fadd_rn(__fmul_rn(a.momentum, m), __fmul_rn(a.omdamp, d)) : d;
+        d = a.nesterov ? __fadd_rn(d, __fmul_rn(a.momentum, m)) : m;
+    }
+    th = __fsub_rn(th, __fmul_rn(a.lr, d));
+}
 
 // One element of AdamW::step (adamw.cpp:151-166) on an unscaled, clipped grad.
 __device__ __forceinline__ void adamw_elem(float& th, float& m, float& v, float g,
@@ -190,7 +205,7 @@ __device__ __forceinline__ float ema_elem(float sh, float w, const ApplyArgs& a)
     return __fadd_rn(__fmul_rn(a.ema_decay, sh), __fmul_rn(a.ema_omd, w));
 }
 
-template <bool kMixed, bool kAg, bool kEma>
+template <bool kMixed, bool kAg, bool kEma, bool kSgd>
 __device__ __forceinline__ void apply_scalar(const Chunk& ch, uint32_t from, uint32_t to,
                                              uint32_t tid, uint32_t nthreads, const ApplyArgs& a,
                                              const StepCoeffs& k, float lr_wd, bool has_wd,
@@ -198,11 +213,19 @@ __device__ __forceinline__ void apply_scalar(const Chunk& ch, uint32_t from, uin
     for (uint32_t i = from + tid; i < to; i += nthreads) {
         const float graw = kMixed ? bf16_bits_to_f32(static_cast<const uint16_t*>(ch.grad)[i])
                                   : static_cast<const float*>(ch.grad)[i];
-        float th = ch.master[i], m = ch.m[i], v = ch.v[i];
-        adamw_elem(th, m, v, prep_grad(graw, k), a, k, lr_wd, has_wd);
-        ch.master[i] = th;
-        ch.m[i] = m;
-        ch.v[i] = v;
+        float th = ch.master[i];
+        if constexpr (kSgd) {
+            float m = a.momentum != 0.0f ? ch.m[i] : 0.0f;
+            sgd_elem(th, m, prep_grad(graw, k), a, k, ch.wd);
+            ch.master[i] = th;
+            if (a.momentum != 0.0f) ch.m[i] = m;
+        } else {
+            float m = ch.m[i], v = ch.v[i];
+            adamw_elem(th, m, v, prep_grad(graw, k), a, k, lr_wd, has_wd);
+            ch.master[i] = th;
+            ch.m[i] = m;
+            ch.v[i] = v;
+        }
         if constexpr (kEma) {
             float* sh = ch.m + a.ema_delta;
             sh[i] = ema_elem(sh[i], th, a);
@@ -239,12 +262,12 @@ __device__ __forceinline__ void for_each_tile(const Chunk* chunks, int n_vec, F&
     }
 }
 
-template <bool kMixed, bool kAg, bool kEma>
+template <bool kMixed, bool kAg, bool kEma, bool kSgd>
 __global__ void __launch_bounds__(kApplyThreads, 1)
 k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restrict__ ctl,
         ApplyArgs a, AgArgs ag) {
     extern __shared__ __align__(128) unsigned char smem[];
-    constexpr int kStages = apply_stages(kMixed, kEma);
+    constexpr int kStages = apply_stages(kMixed, kEma, kSgd);
     __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages];
     __shared__ StepCoeffs s_k;
     __shared__ int s_skip, s_found, s_err, s_drain_err;
@@ -257,10 +280,14 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
 
     constexpr uint32_t kGradBytes = kMixed ? 2u : 4u;
     constexpr uint32_t kVecElems = kVecBytes / kGradBytes;  // elements per 16 B of grad
-    constexpr uint32_t kStage = static_cast<uint32_t>(stage_bytes(kMixed, kEma));
+    constexpr uint32_t kStage = static_cast<uint32_t>(stage_bytes(kMixed, kEma, kSgd));
+    // stage layout: grad | master | m (AdamW m, or the SGD momentum buffer) | v (AdamW) | EMA
     constexpr uint32_t kOffMaster = kGradBytes * kTile, kOffM = kOffMaster + 4u * kTile,
-                       kOffV = kOffM + 4u * kTile, kOffE = kOffV + 4u * kTile;
-    constexpr uint32_t kStreamBytes = kGradBytes + (kEma ? 16u : 12u);  // loaded per element
+                       kOffV = kOffM + 4u * kTile, kOffE = kOffV + (kSgd ? 0u : 4u) * kTile;
+    // SGD without momentum never touches its buffer
+    const bool use_m = !kSgd || a.momentum != 0.0f;
+    const uint32_t stream_bytes =
+        kGradBytes + 4u + (use_m ? 4u : 0u) + (kSgd ? 0u : 4u) + (kEma ? 4u : 0u);
     constexpr int kConsumers = kConsumerWarps * 32;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -287,6 +314,7 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
         k.coef = coef;
         k.step_size = __fdiv_rn(a.lr, bc.x);  // adamw.cpp:130
         k.sqrt_bc2 = bc.y;
+        k.has_buf = ctl->t > 0;  // applied steps so far (skipped steps never fill buffers)
         s_k = k;
         s_skip = skip;
         s_t = t;
@@ -317,14 +345,14 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                         return false;
                     const uint32_t lv = len & ~(kVecElems - 1);
                     const uint32_t fb = smem_u32(&full_bar[s]);
-                    mbar_expect_tx(fb, kStreamBytes * lv);
+                    mbar_expect_tx(fb, stream_bytes * lv);
                     if (lv) {
                         const uint32_t base = smem_u32(smem + s * kStage);
                         bulk_load(base, static_cast<const char*>(ch.grad) + kGradBytes * t0,
                                   kGradBytes * lv, fb);
                         bulk_load(base + kOffMaster, ch.master + t0, 4u * lv, fb);
-                        bulk_load(base + kOffM, ch.m + t0, 4u * lv, fb);
-                        bulk_load(base + kOffV, ch.v + t0, 4u * lv, fb);
+                        if (use_m) bulk_load(base + kOffM, ch.m + t0, 4u * lv, fb);
+                        if constexpr (!kSgd) bulk_load(base + kOffV, ch.v + t0, 4u * lv, fb);
                         if constexpr (kEma) bulk_load(base + kOffE, ch.m + a.ema_delta + t0, 4u * lv, fb);
                     }
                     s_issued = q + 1;
@@ -358,14 +386,24 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                         } else {
                             g = reinterpret_cast<const float4*>(st)[i];
                         }
-                        float4 th = sms[i], mm = sm[i], vv = sv[i];
-                        adamw_elem(th.x, mm.x, vv.x, prep_grad(g.x, k), a, k, lr_wd, has_wd);
-                        adamw_elem(th.y, mm.y, vv.y, prep_grad(g.y, k), a, k, lr_wd, has_wd);
-                        adamw_elem(th.z, mm.z, vv.z, prep_grad(g.z, k), a, k, lr_wd, has_wd);
-                        adamw_elem(th.w, mm.w, vv.w, prep_grad(g.w, k), a, k, lr_wd, has_wd);
+                        float4 th = sms[i];
+                        if constexpr (kSgd) {
+                            float4 mm = use_m ? sm[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+                            sgd_elem(th.x, mm.x, prep_grad(g.x, k), a, k, ch.wd);
+                            sgd_elem(th.y, mm.y, prep_grad(g.y, k), a, k, ch.wd);
+                            sgd_elem(th.z, mm.z, prep_grad(g.z, k), a, k, ch.wd);
+                            sgd_elem(th.w, mm.w, prep_grad(g.w, k), a, k, ch.wd);
+                            if (use_m) sm[i] = mm;
+                        } else {
+                            float4 mm = sm[i], vv = sv[i];
+                            adamw_elem(th.x, mm.x, vv.x, prep_grad(g.x, k), a, k, lr_wd, has_wd);
+                            adamw_elem(th.y, mm.y, vv.y, prep_grad(g.y, k), a, k, lr_wd, has_wd);
+                            adamw_elem(th.z, mm.z, vv.z, prep_grad(g.z, k), a, k, lr_wd, has_wd);
+                            adamw_elem(th.w, mm.w, vv.w, prep_grad(g.w, k), a, k, lr_wd, has_wd);
+                            sm[i] = mm;
+                            sv[i] = vv;
+                        }
                         sms[i] = th;
-                        sm[i] = mm;
-                        sv[i] = vv;
                         if constexpr (kEma) {
                             float4 e = se[i];
                             e.x = ema_elem(e.x, th.x, a);
@@ -383,8 +421,8 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                         }
                     }
                     // the < 16-byte tail of the tile, straight from global memory
-                    apply_scalar<kMixed, kAg, kEma>(ch, t0 + lv, t0 + len, tid, kConsumers, a,
-                                                    k, lr_wd, has_wd, ag);
+                    apply_scalar<kMixed, kAg, kEma, kSgd>(ch, t0 + lv, t0 + len, tid,
+                                                          kConsumers, a, k, lr_wd, has_wd, ag);
                 }
                 // make the stage's generic-proxy writes visible to the bulk store;
                 // after the barrier every consumer reads the same failure flag
@@ -397,8 +435,8 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                         if constexpr (kMixed)
                             bulk_store(static_cast<uint16_t*>(ch.param) + t0, base, 2u * lv);
                         bulk_store(ch.master + t0, base + kOffMaster, 4u * lv);
-                        bulk_store(ch.m + t0, base + kOffM, 4u * lv);
-                        bulk_store(ch.v + t0, base + kOffV, 4u * lv);
+                        if (use_m) bulk_store(ch.m + t0, base + kOffM, 4u * lv);
+                        if constexpr (!kSgd) bulk_store(ch.v + t0, base + kOffV, 4u * lv);
                         if constexpr (kEma) bulk_store(ch.m + a.ema_delta + t0, base + kOffE, 4u * lv);
                         if constexpr (kAg) {
                             // the fused all-gather: the same param tile into every peer
@@ -421,8 +459,8 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
             // scalar chunks (misaligned heads, mixed-phase tensors)
             for (int c = s_err ? n_chunks : n_vec + static_cast<int>(blockIdx.x); c < n_chunks; c += gridDim.x) {
                 const Chunk ch = chunks[c];
-                apply_scalar<kMixed, kAg, kEma>(ch, 0, ch.n, tid, kConsumers, a, k,
-                                                __fmul_rn(a.lr, ch.wd), ch.wd != 0.0f, ag);
+                apply_scalar<kMixed, kAg, kEma, kSgd>(ch, 0, ch.n, tid, kConsumers, a, k,
+                                                      __fmul_rn(a.lr, ch.wd), ch.wd != 0.0f, ag);
             }
         }
     }
@@ -509,22 +547,49 @@ __global__ void k_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float sca
 
 // --------------------------------------------------------------- launchers --
 
+template <bool kMixed, bool kAg, bool kEma, bool kSgd>
+static cudaError_t set_smem_attr() {
+    return cudaFuncSetAttribute(k_apply<kMixed, kAg, kEma, kSgd>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(apply_smem_bytes(kMixed, kEma, kSgd)));
+}
+
+template <bool kMixed, bool kAg, bool kEma, bool kSgd>
+static void launch_apply_t(const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
+                           const ApplyArgs& args, int grid, cudaStream_t stream, const AgArgs& ag) {
+    k_apply<kMixed, kAg, kEma, kSgd>
+        <<<grid, kApplyThreads, apply_smem_bytes(kMixed, kEma, kSgd), stream>>>(
+            chunks, n_chunks, n_vec, ctl, args, ag);
+}
+
+// The 16 instantiations, indexed by (mixed, ag, ema, sgd) bits.
+using SetFn = cudaError_t (*)();
+using LaunchFn = void (*)(const Chunk*, int, int, Ctl*, const ApplyArgs&, int, cudaStream_t,
+                          const AgArgs&);
+#define SOARB_VARIANT(b)                                                                      \
+    {set_smem_attr<(b & 8) != 0, (b & 4) != 0, (b & 2) != 0, (b & 1) != 0>,                   \
+     launch_apply_t<(b & 8) != 0, (b & 4) != 0, (b & 2) != 0, (b & 1) != 0>}
+struct Variant {
+    SetFn set;
+    LaunchFn launch;
+};
+static const Variant kVariants[16] = {
+    SOARB_VARIANT(0),  SOARB_VARIANT(1),  SOARB_VARIANT(2),  SOARB_VARIANT(3),
+    SOARB_VARIANT(4),  SOARB_VARIANT(5),  SOARB_VARIANT(6),  SOARB_VARIANT(7),
+    SOARB_VARIANT(8),  SOARB_VARIANT(9),  SOARB_VARIANT(10), SOARB_VARIANT(11),
+    SOARB_VARIANT(12), SOARB_VARIANT(13), SOARB_VARIANT(14), SOARB_VARIANT(15)};
+#undef SOARB_VARIANT
+
+static int variant_index(bool mixed, bool ag, bool ema, bool sgd) {
+    return (mixed ? 8 : 0) | (ag ? 4 : 0) | (ema ? 2 : 0) | (sgd ? 1 : 0);
+}
+
 cudaError_t prepare_kernels() {
-    cudaError_t e = cudaSuccess;
-    auto set = [&](auto kern, bool mixed, bool ema) {
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(apply_smem_bytes(mixed, ema)));
-    };
-    set(k_apply<true, false, false>, true, false);
-    set(k_apply<false, false, false>, false, false);
-    set(k_apply<true, true, false>, true, false);
-    set(k_apply<false, true, false>, false, false);
-    set(k_apply<true, false, true>, true, true);
-    set(k_apply<false, false, true>, false, true);
-    set(k_apply<true, true, true>, true, true);
-    set(k_apply<false, true, true>, false, true);
-    return e;
+    for (const Variant& v : kVariants) {
+        const cudaError_t e = v.set();
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl* ctl,
@@ -539,29 +604,12 @@ cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl*
     return cudaGetLastError();
 }
 
-template <bool kMixed, bool kAg, bool kEma>
-static void launch_apply_t(const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
-                           const ApplyArgs& args, int grid, cudaStream_t stream, const AgArgs& ag) {
-    k_apply<kMixed, kAg, kEma><<<grid, kApplyThreads, apply_smem_bytes(kMixed, kEma), stream>>>(
-        chunks, n_chunks, n_vec, ctl, args, ag);
-}
-
 cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
                          const ApplyArgs& args, int grid, cudaStream_t stream, const AgArgs* ag,
-                         bool ema) {
+                         bool ema, bool sgd) {
     const AgArgs none{};
-    const AgArgs& g = ag ? *ag : none;
-    const int sel = (mixed ? 4 : 0) | (ag ? 2 : 0) | (ema ? 1 : 0);
-    switch (sel) {
-        case 0: launch_apply_t<false, false, false>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
-        case 1: launch_apply_t<false, false, true>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
-        case 2: launch_apply_t<false, true, false>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
-        case 3: launch_apply_t<false, true, true>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
-        case 4: launch_apply_t<true, false, false>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
-        case 5: launch_apply_t<true, false, true>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
-        case 6: launch_apply_t<true, true, false>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
-        default: launch_apply_t<true, true, true>(chunks, n_chunks, n_vec, ctl, args, grid, stream, g); break;
-    }
+    kVariants[variant_index(mixed, ag != nullptr, ema, sgd)].launch(
+        chunks, n_chunks, n_vec, ctl, args, grid, stream, ag ? *ag : none);
     return cudaGetLastError();
 }
 
@@ -604,20 +652,27 @@ int occupancy_grad_sumsq(bool bf16) {
     return n > 0 ? n : 1;
 }
 
-int occupancy_apply(bool mixed, bool ema) {
+template <bool kMixed, bool kEma, bool kSgd>
+static int occupancy_t() {
     int n = 0;
-    if (mixed && ema)
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<true, false, true>, kApplyThreads,
-                                                      apply_smem_bytes(true, true));
-    else if (mixed)
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<true, false, false>,
-                                                      kApplyThreads, apply_smem_bytes(true));
-    else if (ema)
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<false, false, true>,
-                                                      kApplyThreads, apply_smem_bytes(false, true));
-    else
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<false, false, false>,
-                                                      kApplyThreads, apply_smem_bytes(false));
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<kMixed, false, kEma, kSgd>,
+                                                  kApplyThreads,
+                                                  apply_smem_bytes(kMixed, kEma, kSgd));
+    return n;
+}
+
+int occupancy_apply(bool mixed, bool ema, bool sgd) {
+    int n;
+    switch ((mixed ? 4 : 0) | (ema ? 2 : 0) | (sgd ? 1 : 0)) {
+        case 0: n = occupancy_t<false, false, false>(); break;
+        case 1: n = occupancy_t<false, false, true>(); break;
+        case 2: n = occupancy_t<false, true, false>(); break;
+        case 3: n = occupancy_t<false, true, true>(); break;
+        case 4: n = occupancy_t<true, false, false>(); break;
+        case 5: n = occupancy_t<true, false, true>(); break;
+        case 6: n = occupancy_t<true, true, false>(); break;
+        default: n = occupancy_t<true, true, true>(); break;
+    }
     return n > 0 ? n : 1;
 }
 

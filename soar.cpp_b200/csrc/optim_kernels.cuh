@@ -73,6 +73,10 @@ struct ApplyArgs {
     // fused weight EMA (ModelEMA::update): shadow = decay*shadow + (1-decay)*weight
     float ema_decay, ema_omd; // decay and (1 - decay) rounded as the reference's float expression
     long long ema_delta;      // element offset from a chunk's m pointer to its shadow pointer
+    // SGD (the chunk's m pointer is the momentum buffer; v is unused)
+    float momentum;
+    float omdamp;             // 1 - dampening, rounded as the reference's float expression
+    int32_t nesterov;
 };
 
 // Data-parallel all-gather fused into the update: after a tile of the rank's
@@ -94,18 +98,20 @@ constexpr int kTile = 1024;
 constexpr int kMaxStages = 6;
 constexpr int kConsumerWarps = 12;
 constexpr int kApplyThreads = (kConsumerWarps + 1) * 32;
-// bytes of one pipeline stage: grad tile + master, m, v (+ EMA shadow) tiles
-__host__ __device__ constexpr size_t stage_bytes(bool mixed, bool ema = false) {
-    return (mixed ? 2u : 4u) * kTile + (ema ? 16u : 12u) * kTile;
+// bytes of one pipeline stage: grad tile + master, m, v (AdamW) or master,
+// momentum (SGD) tiles, + the EMA shadow tile
+__host__ __device__ constexpr size_t stage_bytes(bool mixed, bool ema = false, bool sgd = false) {
+    return (mixed ? 2u : 4u) * kTile + (sgd ? 8u : 12u) * kTile + (ema ? 4u : 0u) * kTile;
 }
 // stages that keep two CTAs per SM (<= ~108 KB of ring each)
-__host__ __device__ constexpr int apply_stages(bool mixed, bool ema = false) {
-    return static_cast<int>(110592 / stage_bytes(mixed, ema)) < kMaxStages
-               ? static_cast<int>(110592 / stage_bytes(mixed, ema))
+__host__ __device__ constexpr int apply_stages(bool mixed, bool ema = false, bool sgd = false) {
+    return static_cast<int>(110592 / stage_bytes(mixed, ema, sgd)) < kMaxStages
+               ? static_cast<int>(110592 / stage_bytes(mixed, ema, sgd))
                : kMaxStages;
 }
-__host__ __device__ constexpr size_t apply_smem_bytes(bool mixed, bool ema = false) {
-    return stage_bytes(mixed, ema) * apply_stages(mixed, ema);
+__host__ __device__ constexpr size_t apply_smem_bytes(bool mixed, bool ema = false,
+                                                      bool sgd = false) {
+    return stage_bytes(mixed, ema, sgd) * apply_stages(mixed, ema, sgd);
 }
 
 // Launchers (optim_kernels.cu). Each returns the launch status.
@@ -113,10 +119,11 @@ cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl*
                               double* partials, int grid, int use_scaler, double* out,
                               cudaStream_t stream);
 // ag == nullptr: plain update; otherwise the update with the fused all-gather.
-// ema: also update the weight EMA shadow (args.ema_*).
+// ema: also update the weight EMA shadow (args.ema_*). sgd: the SGD update
+// (args.momentum/omdamp/nesterov) instead of AdamW.
 cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
                          const ApplyArgs& args, int grid, cudaStream_t stream,
-                         const AgArgs* ag = nullptr, bool ema = false);
+                         const AgArgs* ag = nullptr, bool ema = false, bool sgd = false);
 cudaError_t launch_scale_grads_f32(const Chunk* chunks, int n_chunks, float coef, int grid,
                                    cudaStream_t stream);
 cudaError_t launch_bf16_to_f32(const uint16_t* src, float* dst, uint64_t n,
@@ -131,7 +138,7 @@ cudaError_t prepare_kernels();
 
 // Resident CTAs per SM of each kernel at its launch configuration.
 int occupancy_grad_sumsq(bool bf16);
-int occupancy_apply(bool mixed, bool ema = false);
+int occupancy_apply(bool mixed, bool ema = false, bool sgd = false);
 
 constexpr int kThreads = 256;
 

@@ -45,6 +45,15 @@ class AdamWOpts(C.Structure):
                 ("device", C.c_int32)]
 
 
+class SGDOpts(C.Structure):
+    _fields_ = [("lr", C.c_float), ("momentum", C.c_float), ("dampening", C.c_float),
+                ("weight_decay", C.c_float), ("nesterov", C.c_int32), ("layout", C.c_int32),
+                ("max_grad_norm", C.c_float), ("use_loss_scaler", C.c_int32),
+                ("init_scale", C.c_float), ("growth_factor", C.c_float),
+                ("backoff_factor", C.c_float), ("growth_interval", C.c_int32),
+                ("device", C.c_int32)]
+
+
 class StepInfo(C.Structure):
     _fields_ = [("step", C.c_uint64), ("skipped", C.c_uint64), ("grad_norm", C.c_float),
                 ("found_inf", C.c_int32), ("clip_coef", C.c_float), ("loss_scale", C.c_float),
@@ -65,6 +74,9 @@ SIGNATURES: dict[str, tuple] = {
                                             C.POINTER(C.c_uint64), C.c_int,
                                             C.POINTER(AdamWOpts), C.POINTER(C.c_void_p)]),
     "soar_optim_destroy": (C.c_int, [C.c_void_p]),
+    "soar_sgd_default_opts": (None, [C.POINTER(SGDOpts)]),
+    "soar_sgd_create": (C.c_int, [C.POINTER(TensorDesc), C.c_int, C.POINTER(SGDOpts),
+                                  C.POINTER(C.c_void_p)]),
     "soar_optim_step": (C.c_int, [C.c_void_p, C.c_void_p]),
     "soar_optim_clip_grad_norm": (C.c_int, [C.c_void_p, C.c_float, C.POINTER(C.c_float),
                                             C.c_void_p]),
@@ -171,6 +183,17 @@ class AdamWOptions:
 
 
 @dataclass
+class SGDOptions:
+    """include/soar/optim/sgd.hpp:9-15, same defaults."""
+
+    lr: float = 1e-2
+    momentum: float = 0.0
+    dampening: float = 0.0
+    weight_decay: float = 0.0
+    nesterov: bool = False
+
+
+@dataclass
 class LossScalerOptions:
     """Dynamic loss scaler (no reference counterpart)."""
 
@@ -203,16 +226,25 @@ class AdamW:
                  max_grad_norm: float = 0.0, loss_scaler: LossScalerOptions | None = None,
                  device: int | None = None, grads=None):
         options = options or AdamWOptions()
+        o = AdamWOpts()
+        lib().soar_adamw_default_opts(C.byref(o))
+        o.lr, o.beta1, o.beta2, o.eps = options.lr, options.beta1, options.beta2, options.eps
+        o.weight_decay = options.weight_decay
+        self._create(params, grads, options.weight_decay, o, layout, max_grad_norm, loss_scaler,
+                     device, lib().soar_optim_create, "soar_optim_create")
+
+    def _create(self, params, grads, default_wd, o, layout, max_grad_norm, loss_scaler, device,
+                create_fn, create_name):
         tensors, wds = [], []
         for p in params:
             if isinstance(p, ParamGroup):
-                wd = options.weight_decay if p.weight_decay is None else p.weight_decay
+                wd = default_wd if p.weight_decay is None else p.weight_decay
                 for q in p.params:
                     tensors.append(q)
                     wds.append(wd)
             else:
                 tensors.append(p)
-                wds.append(options.weight_decay)
+                wds.append(default_wd)
         self.params = tensors
         # gradients: explicit list (same order as the flattened params) or .grad
         self.grads = list(grads) if grads is not None else [getattr(p, "grad", None)
@@ -220,10 +252,6 @@ class AdamW:
         if len(self.grads) != len(tensors):
             raise ValueError("one gradient (or None) per parameter")
         self.layout = {"fp32": LAYOUT_FP32, "bf16_mixed": LAYOUT_BF16_MIXED}[layout]
-        o = AdamWOpts()
-        lib().soar_adamw_default_opts(C.byref(o))
-        o.lr, o.beta1, o.beta2, o.eps = options.lr, options.beta1, options.beta2, options.eps
-        o.weight_decay = options.weight_decay
         o.layout = self.layout
         o.max_grad_norm = max_grad_norm
         if loss_scaler is not None:
@@ -248,7 +276,7 @@ class AdamW:
         self.numel = [p.numel() for p in tensors]
         self.weight_decays = wds
         h = C.c_void_p()
-        _check(lib().soar_optim_create(descs, n, C.byref(o), C.byref(h)), "soar_optim_create")
+        _check(create_fn(descs, n, C.byref(o), C.byref(h)), create_name)
         self.handle = h
 
     def close(self):
@@ -356,6 +384,24 @@ class AdamW:
     def apply(self, parts_ptr: int | None, n_parts: int, stream=None) -> None:
         _check(lib().soar_optim_apply(self.handle, parts_ptr, n_parts, _stream_handle(stream)),
                "soar_optim_apply")
+
+
+class SGD(AdamW):
+    """soar::optim::SGD (include/soar/optim/sgd.hpp:21-38) on the same fused
+    device step: momentum, dampening, Nesterov, coupled weight decay (per
+    ParamGroup), with the same layouts, fused clip and loss scaler. The
+    momentum buffer is state kind STATE_M; there is no STATE_V."""
+
+    def __init__(self, params, options: SGDOptions | None = None, *, layout: str = "fp32",
+                 max_grad_norm: float = 0.0, loss_scaler: LossScalerOptions | None = None,
+                 device: int | None = None, grads=None):
+        options = options or SGDOptions()
+        o = SGDOpts()
+        lib().soar_sgd_default_opts(C.byref(o))
+        o.lr, o.momentum, o.dampening = options.lr, options.momentum, options.dampening
+        o.weight_decay, o.nesterov = options.weight_decay, int(options.nesterov)
+        self._create(params, grads, options.weight_decay, o, layout, max_grad_norm, loss_scaler,
+                     device, lib().soar_sgd_create, "soar_sgd_create")
 
 
 class CosineAnnealingLR:

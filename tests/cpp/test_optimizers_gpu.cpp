@@ -73,6 +73,31 @@ void test_adamw_parity() {
     CHECK(std::fabs(actual - 0.99899f) < 1e-6f, "adamw parity %.9g", actual);
 }
 
+void test_sgd_parity() {
+    // tests/test_optimizers.cpp:51-95. The reference swaps in a new grad
+    // tensor for step 2 (set_grad); this API binds each gradient buffer at
+    // construction -- in training the reference's autograd also accumulates
+    // into one stable grad tensor (tensor.cpp:173-192) -- so step 2's
+    // gradient is written into the bound buffer instead.
+    auto p = make({2.0f});
+    auto g = make({0.4f});
+    p->set_grad(g);
+    soar::optim::SGDOptions opt;
+    opt.lr = 0.1f;
+    opt.momentum = 0.9f;
+    opt.weight_decay = 0.01f;
+    soar::optim::SGD optimizer(std::vector<TensorPtr>{p}, opt);
+    optimizer.step();
+    const float a1 = p->host()[0];
+    CHECK(std::fabs(a1 - 1.958f) < 1e-6f, "sgd step 1 %.9g", a1);
+    const float two = 0.2f;
+    cudaMemcpy(g->cuda_data(), &two, sizeof two, cudaMemcpyHostToDevice);
+    optimizer.step();
+    const float a2 = p->host()[0];
+    std::printf("  SGD step 2: actual = %.9g, expected = 1.898242\n", a2);
+    CHECK(std::fabs(a2 - 1.898242f) < 1e-6f, "sgd step 2 %.9g", a2);
+}
+
 void test_gradient_clipping() {
     // tests/test_optimizers.cpp:97-119
     auto p = make({3.0f, 4.0f});
@@ -120,6 +145,7 @@ int main() {
     }
     std::printf("=== SOAR optimizer tests on the B200 C++ API ===\n");
     test_adamw_parity();
+    test_sgd_parity();
     test_gradient_clipping();
     test_trainer_sequence_and_move();
     if (g_failures) {

@@ -244,3 +244,39 @@ def test_ema_port_matches_reference_bitexact(ref_oracle):
             o.port().oracle_ema_update(sh, w, w.size, 0.999)
     for i, sh in enumerate(shadow):
         np.testing.assert_array_equal(sh.view(np.uint32), e.shadow(i).view(np.uint32))
+
+
+def test_kat_sgd_parity_ref(ref_oracle):
+    """tests/test_optimizers.cpp:51-95: p=2, lr 0.1, momentum 0.9, wd 0.01;
+    g=0.4 -> 1.958, then g=0.2 -> 1.898242 (1e-6)."""
+    o = ref_oracle
+    p = np.array([2.0], np.float32)
+    g = np.array([0.4], np.float32)
+    r = o.RefSGD([p], [g], lr=0.1, momentum=0.9, weight_decay=0.01)
+    r.step()
+    assert abs(p[0] - np.float32(1.958)) < 1e-6
+    g[0] = 0.2
+    r.step()
+    assert abs(p[0] - np.float32(1.898242)) < 1e-6
+
+
+@pytest.mark.parametrize("momentum,dampening,nesterov,wd", [
+    (0.0, 0.0, False, 0.0), (0.9, 0.0, False, 0.01), (0.9, 0.1, False, 0.0),
+    (0.9, 0.0, True, 0.05), (0.5, 0.25, True, 0.0)])
+def test_sgd_port_matches_reference_bitexact(ref_oracle, momentum, dampening, nesterov, wd):
+    o = ref_oracle
+    sizes = [1, 7, 1000, 4099]
+    p_ref = [synth.normal(synth.seed_of(80, i), n, 0.5) for i, n in enumerate(sizes)]
+    g_ref = [np.zeros(n, np.float32) for n in sizes]
+    r = o.RefSGD(p_ref, g_ref, lr=0.05, momentum=momentum, dampening=dampening,
+                 weight_decay=wd, nesterov=nesterov)
+    port = o.PortSGD([p.copy() for p in p_ref], [wd] * len(sizes),
+                     o.StepConfig(layout=0, lr=0.05), momentum, dampening, nesterov)
+    for t in range(1, 5):
+        gs = [synth.normal(synth.seed_of(81, i, t), n, 0.1) for i, n in enumerate(sizes)]
+        for dst, src in zip(g_ref, gs):
+            dst[:] = src
+        r.step()
+        port.step(gs)
+    for a, b in zip(port.params, p_ref):
+        np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
