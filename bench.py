@@ -279,6 +279,33 @@ def run_ours(args):
 
     ms = start.elapsed_time(end)
     apply_ms = [a.elapsed_time(b) for a, b in apply_ev]
+
+    # per-phase breakdown (a separate loop after the timed region, not part of
+    # `value`): CUDA events around each phase of the step on this rank
+    phase_names = (["barrier", "reduce_scatter+sumsq", "partial_allgather", "update+allgather",
+                    "barrier2"] if fused else
+                   ["reduce_scatter", "sumsq+partial_allgather", "update", "param_allgather"])
+    pev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(phase_names) + 1)]
+           for _ in range(10)]
+    for ev in pev:
+        ev[0].record(stream)
+        if fused:
+            z.barrier(); ev[1].record(stream)
+            z.reduce(); ev[2].record(stream)
+            parts = z.gather_partials(); ev[3].record(stream)
+            z.update(parts); ev[4].record(stream)
+            z.barrier(); ev[5].record(stream)
+        else:
+            z.reduce_scatter(); ev[1].record(stream)
+            parts = z.norm_partials(); ev[2].record(stream)
+            z.update(parts); ev[3].record(stream)
+            z.all_gather(); ev[4].record(stream)
+    torch.cuda.synchronize()
+    ph = torch.tensor([statistics.mean(e[i].elapsed_time(e[i + 1]) for e in pev)
+                       for i in range(len(phase_names))], dtype=torch.float64, device=dev)
+    if comm:
+        torch.distributed.all_reduce(ph, op=torch.distributed.ReduceOp.MAX)
+    phases = {k: round(float(v), 4) for k, v in zip(phase_names, ph.tolist())}
     t = torch.tensor([ms, statistics.mean(apply_ms)], dtype=torch.float64, device=dev)
     if comm:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -356,6 +383,7 @@ def run_ours(args):
                 "ms_per_step": e2e_ms / args.e2e_steps},
         "clocks": clock_info,
         "gpu_launches": launches_per_step * args.steps,
+        "phases_ms": phases,
         "final_info": {"step": info.step, "skipped": info.skipped, "loss_scale": info.loss_scale,
                        "grad_norm": info.grad_norm},
     }

@@ -316,6 +316,14 @@ SOAR_API int soar_grad_sumsq_noalloc(const void* const* grads, const uint64_t* n
                                      int n_tensors, int layout, float inv_scale,
                                      double* d_sumsq, void* stream);
 
+/* Failure-detection self-test (no reference counterpart): runs the bounded
+   wait that every device pipeline uses on an mbarrier nothing arrives at,
+   with the given limit, on `device`. *out_timed_out is 1 when the wait gave up
+   and reported it (the expected result), *out_waited_ns how long it waited.
+   No fault, trap or hang is involved; the context stays usable. */
+SOAR_API int soar_selftest_bounded_wait(uint64_t limit_ns, int device, int* out_timed_out,
+                                        uint64_t* out_waited_ns);
+
 /* Message of the calling thread's last failed call ("" if none). */
 SOAR_API const char* soar_last_error(void);
 

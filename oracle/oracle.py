@@ -28,6 +28,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 PORT_SO = HERE / "liboracle_port.so"
 REF_SO = HERE / "_ref" / "libsoar_ref_adamw.so"
+REF_CUDA_SO = HERE / "_ref" / "libsoar_ref_cuda.so"
 REF_ROOT = Path(os.environ.get("SOAR_REF_ROOT", "/root/reference"))
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
@@ -40,11 +41,27 @@ def build(ref: bool | None = None) -> None:
     if ref is None:
         ref = (REF_ROOT / "src" / "optim" / "adamw.cpp").exists()
     if ref:
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF_ROOT={REF_ROOT}"], check=True)
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", "refcuda", f"REF_ROOT={REF_ROOT}"],
+                       check=True)
 
 
 def ref_available() -> bool:
     return REF_SO.exists()
+
+
+def ref_cuda():
+    """The reference's CUDA AdamW kernels for sm_100a (secondary GPU baseline)."""
+    if not REF_CUDA_SO.exists():
+        raise FileNotFoundError(f"{REF_CUDA_SO} not built (needs the reference sources)")
+    lib = C.CDLL(str(REF_CUDA_SO))
+    lib.soar_refcuda_adamw_multi_tensor.argtypes = [
+        C.POINTER(C.c_void_p), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p),
+        C.POINTER(C.c_void_p), C.POINTER(C.c_int64), C.c_int, C.c_float, C.c_float, C.c_float,
+        C.c_float, C.c_float, C.c_float, C.c_float, C.c_void_p]
+    lib.soar_refcuda_adamw_step.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                            C.c_float, C.c_float, C.c_float, C.c_float, C.c_float,
+                                            C.c_float, C.c_float, C.c_uint64, C.c_void_p]
+    return lib
 
 
 class StepState(C.Structure):

@@ -1016,6 +1016,27 @@ SOAR_API int soar_cosine_destroy(void* sched_handle) {
     return SOAR_OK;
 }
 
+SOAR_API int soar_selftest_bounded_wait(uint64_t limit_ns, int device, int* out_timed_out,
+                                        uint64_t* out_waited_ns) {
+    if (!out_timed_out || !out_waited_ns) return fail("null argument");
+    DeviceGuard g(device);
+    if (!g.ok) return fail("cannot select device");
+    int* d_err = nullptr;
+    SOAR_CUDA_TRY(cudaMalloc(&d_err, 64));
+    unsigned long long* d_ns = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(d_err) + 32);
+    cudaError_t e = soarb::launch_wait_selftest(limit_ns, d_err, d_ns, nullptr);
+    int err = 0;
+    unsigned long long ns = 0;
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(&err, d_err, sizeof err, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(&ns, d_ns, sizeof ns, cudaMemcpyDeviceToHost);
+    cudaFree(d_err);
+    if (e != cudaSuccess) return fail(std::string("selftest: ") + cudaGetErrorString(e));
+    *out_timed_out = err;
+    *out_waited_ns = ns;
+    return SOAR_OK;
+}
+
 SOAR_API const char* soar_last_error(void) { return g_last_error.c_str(); }
 
 }  // extern "C"

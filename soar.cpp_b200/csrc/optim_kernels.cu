@@ -534,6 +534,25 @@ __global__ void k_f32_to_bf16(const float* __restrict__ src, uint16_t* __restric
         dst[i] = f32_to_bf16_rn(src[i]);
 }
 
+// Self-test of the bounded wait every pipeline uses: one thread waits on an
+// mbarrier that nothing will ever arrive at, with a short limit, and reports
+// whether it gave up and how long it waited. Nothing faults or hangs.
+__global__ void k_wait_selftest(uint64_t limit_ns, int* out_error, unsigned long long* out_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int s_err;
+    if (threadIdx.x == 0) {
+        s_err = 0;
+        mbar_init(smem_u32(&bar), 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        const uint64_t t0 = global_timer_ns();
+        const bool ok = mbar_wait(smem_u32(&bar), 0, &s_err, limit_ns);  // phase 0 never completes
+        *out_ns = global_timer_ns() - t0;
+        *out_error = ok ? 0 : s_err;
+        // retire the barrier's pending phase so the CTA exits with it consistent
+        mbar_arrive(smem_u32(&bar));
+    }
+}
+
 __global__ void k_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float scale,
                                int32_t tracker) {
     ctl->t = t;
@@ -640,6 +659,12 @@ cudaError_t launch_f32_to_bf16(const float* src, uint16_t* dst, uint64_t n,
 cudaError_t launch_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float scale,
                                 int32_t tracker, cudaStream_t stream) {
     k_set_counters<<<1, 1, 0, stream>>>(ctl, t, skipped, scale, tracker);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_wait_selftest(uint64_t limit_ns, int* out_error, unsigned long long* out_ns,
+                                 cudaStream_t stream) {
+    k_wait_selftest<<<1, 32, 0, stream>>>(limit_ns, out_error, out_ns);
     return cudaGetLastError();
 }
 

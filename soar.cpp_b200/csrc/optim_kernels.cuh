@@ -133,6 +133,9 @@ cudaError_t launch_f32_to_bf16(const float* src, uint16_t* dst, uint64_t n,
 cudaError_t launch_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float scale,
                                 int32_t tracker, cudaStream_t stream);
 
+cudaError_t launch_wait_selftest(uint64_t limit_ns, int* out_error, unsigned long long* out_ns,
+                                 cudaStream_t stream);
+
 // One-time per-process kernel attribute set-up (dynamic shared memory size).
 cudaError_t prepare_kernels();
 

@@ -59,14 +59,17 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 }
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s
 
-// Bounded wait for the phase of `bar` with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* s_err) {
+// Bounded wait for the phase of `bar` with the given parity to complete. Gives
+// up after limit_ns of %globaltimer (setting *s_err), or as soon as another
+// thread has set *s_err.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* s_err,
+                                          uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try(bar, parity)) return true;
         if ((i & 1023u) == 0) {
-            if (global_timer_ns() - t0 > kWaitLimitNs) {
+            if (global_timer_ns() - t0 > limit_ns) {
                 atomicOr(s_err, 1);
                 return false;
             }

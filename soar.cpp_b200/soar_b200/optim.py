@@ -114,6 +114,8 @@ SIGNATURES: dict[str, tuple] = {
     "soar_zero1_apply_allgather": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
     "soar_zero1_error": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
     "soar_zero1_destroy": (C.c_int, [C.c_void_p]),
+    "soar_selftest_bounded_wait": (C.c_int, [C.c_uint64, C.c_int, C.POINTER(C.c_int),
+                                             C.POINTER(C.c_uint64)]),
     "soar_last_error": (C.c_char_p, []),
 }
 
