@@ -6,7 +6,9 @@ global-norm clip 1.0, dynamic loss scaler, lr 1e-3, wd 0.01. At N GPUs each
 rank brings its own full 200M-element gradient; a step reduce-scatters it, runs
 the fused unscale/norm/clip/AdamW on the rank's 1/N shard and all-gathers the
 bf16 params -- by default with both collectives fused into the kernels over
-peer memory (--dp fused), or with NCCL around the kernels (--dp nccl). Unit:
+peer memory and the ranks synchronised by device-side flags (--dp fused; with
+small NCCL collectives as the synchronisation instead: --dp fused-nccl), or
+with NCCL around the kernels (--dp nccl). Unit:
 one parameter-gradient of one rank reduced and applied, so each GPU's input is
 fixed as N grows ("weak"); at N = 1 it is simply parameters updated per
 second.
@@ -65,9 +67,11 @@ def parse():
                     help="config 5: flat 1M..2B params in both layouts, one JSON line each "
                          "(not the headline line)")
     ap.add_argument("--sweep-sizes", default="1000000,16000000,256000000,1000000000,2000000000")
-    ap.add_argument("--dp", default="fused", choices=["fused", "nccl"],
-                    help="N>1: collectives fused into the kernels over peer memory (default) "
-                         "or NCCL reduce-scatter / all-gather around the kernels")
+    ap.add_argument("--dp", default="fused", choices=["fused", "fused-nccl", "nccl"],
+                    help="N>1: collectives fused into the kernels over peer memory, the ranks "
+                         "synchronised by device-side flags (default) or by small NCCL "
+                         "collectives between the launches (fused-nccl); or NCCL "
+                         "reduce-scatter / all-gather around the kernels (nccl)")
     return ap.parse_args()
 
 
@@ -218,13 +222,16 @@ def run_ours(args):
                         loss_scaler=sb.LossScalerOptions(init_scale=65536.0), grads=sg,
                         device=local)
 
-    fused = world > 1 and args.dp == "fused"
+    fused = world > 1 and args.dp.startswith("fused")
+    dev_sync = fused and args.dp == "fused"
     if fused:
-        z = dp.FusedZeroOneAdamW(n, BUCKET, make_opt, device=local, init_params=params)
+        z = dp.FusedZeroOneAdamW(n, BUCKET, make_opt, device=local, init_params=params,
+                                 sync="device" if dev_sync else "nccl")
         del params, grads
         params, grads = z.params, z.grads
         grads.copy_(torch.from_numpy(g_host.view(np.int16)).view(torch.bfloat16).to(dev))
-        launches_per_step = 2
+        # k_rs_sumsq, k_apply<all-gather> (+ the end-of-step flag wait)
+        launches_per_step = 3 if dev_sync else 2
     else:
         z = dp.ZeroOneAdamW(params, grads, BUCKET, make_opt, comm)
         launches_per_step = 2
@@ -236,6 +243,9 @@ def run_ours(args):
             torch.distributed.barrier(device_ids=[local])
 
     def one_step(ev=None):
+        if dev_sync:
+            z.step()  # one call: no host collective, so no event inside the step
+            return
         if fused:
             z.barrier()
             z.reduce()
@@ -278,15 +288,18 @@ def run_ours(args):
     clock_info = clocks.stop(list(range(world))) if clocks else None
 
     ms = start.elapsed_time(end)
-    apply_ms = [a.elapsed_time(b) for a, b in apply_ev]
+    apply_ms = None if dev_sync else [a.elapsed_time(b) for a, b in apply_ev]
 
     # per-phase breakdown (a separate loop after the timed region, not part of
-    # `value`): CUDA events around each phase of the step on this rank
+    # `value`): CUDA events around each phase of the step on this rank (the
+    # fused path runs its caller-synchronised form here, so the phases split)
     phase_names = (["barrier", "reduce_scatter+sumsq", "partial_allgather", "update+allgather",
                     "barrier2"] if fused else
                    ["reduce_scatter", "sumsq+partial_allgather", "update", "param_allgather"])
     pev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(phase_names) + 1)]
            for _ in range(10)]
+    barrier()  # (rank 0 stopped the clock sampler: start the ranks together)
+    torch.cuda.synchronize()
     for ev in pev:
         ev[0].record(stream)
         if fused:
@@ -306,6 +319,8 @@ def run_ours(args):
     if comm:
         torch.distributed.all_reduce(ph, op=torch.distributed.ReduceOp.MAX)
     phases = {k: round(float(v), 4) for k, v in zip(phase_names, ph.tolist())}
+    if apply_ms is None:  # device-synchronised step: the update phase of the loop above
+        apply_ms = [float(ph[phase_names.index("update+allgather")])]
     t = torch.tensor([ms, statistics.mean(apply_ms)], dtype=torch.float64, device=dev)
     if comm:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -367,7 +382,10 @@ def run_ours(args):
                                "fp32 master/m/v, 25M buckets, clip 1.0, loss scaler 65536",
                    "params": n, "bucket": BUCKET, "params_per_rank_shard": shard_params,
                    "parallelism": f"dp{world} zero1" + (
-                       " (collectives fused into the kernels over peer memory)" if fused else
+                       " (collectives fused into the kernels over peer memory, device-side "
+                       "flag synchronisation)" if dev_sync else
+                       " (collectives fused into the kernels over peer memory, NCCL "
+                       "synchronisation)" if fused else
                        " (NCCL reduce-scatter/all-gather)" if world > 1 else ""),
                    "global_batch": None, "seq_len": None,
                    "l2": "inputs larger than L2 (16 B/param resident state = "

@@ -245,6 +245,7 @@ SOAR_API int soar_optim_apply(void* handle, const double* d_parts, int n_parts, 
    identical element offsets. */
 #define SOAR_IPC_HANDLE_BYTES 64
 
+/* Allocations are zero-filled. */
 SOAR_API int soar_ipc_alloc(size_t bytes, int device, void** out_ptr, void* out_handle);
 SOAR_API int soar_ipc_free(void* ptr, int device);
 SOAR_API int soar_ipc_open(const void* handle, int device, void** out_peer_ptr);
@@ -280,8 +281,30 @@ SOAR_API int soar_zero1_reduce_sumsq(void* zero1_handle, double* d_partial, void
 SOAR_API int soar_zero1_apply_allgather(void* zero1_handle, const double* d_parts, int n_parts,
                                         void* stream);
 
-/* Nonzero in *out_error if a device-side wait of the reduce-scatter timed out
-   (synchronises the device). */
+/* Device-synchronised step. signal_bases[q]: rank q's signal block (at least
+   SOAR_ZERO1_SIGNAL_BYTES, 256-byte aligned, zero-filled: one soar_ipc_alloc
+   per rank, opened by every other rank like the buffers; index `rank` is the
+   local one). Set once per handle, before its first soar_zero1_step, and
+   every rank's block must be allocated (zeroed) before any rank steps; a block
+   serves one handle for its lifetime. */
+#define SOAR_ZERO1_SIGNAL_BYTES 4096
+SOAR_API int soar_zero1_set_signals(void* zero1_handle, void* const* signal_bases);
+
+/* The whole data-parallel step with no host collective: the reduce-scatter
+   with the norm pass, the exchange of the R partial sums, the update with the
+   all-gather and the end-of-step wait, synchronised across GPUs by epoch flags
+   in the signal blocks (system-scope release / acquire, every wait bounded to
+   1 s). Stream-ordered like soar_optim_step: it starts after this rank's
+   earlier work on `stream` (the gradients) and, when it completes, every
+   rank's parameter writes into this rank's buffer have landed. Every rank
+   calls it once per step. A timed-out wait skips the step's update (counted
+   as a skipped step) and sets the error flag (soar_zero1_error); after that
+   the ranks' optimizer states may differ and training resumes from a
+   checkpoint. */
+SOAR_API int soar_zero1_step(void* zero1_handle, void* stream);
+
+/* Nonzero in *out_error if a device-side wait of the data-parallel step timed
+   out (synchronises the device). */
 SOAR_API int soar_zero1_error(void* zero1_handle, int* out_error);
 SOAR_API int soar_zero1_destroy(void* zero1_handle);
 

@@ -457,11 +457,12 @@ soarb::ApplyArgs apply_args(const Optim& o, const double* parts, int n_parts) {
 }
 
 int apply_impl(Optim& o, const double* parts, int n_parts, cudaStream_t s,
-               const soarb::AgArgs* ag = nullptr) {
+               const soarb::AgArgs* ag = nullptr, const int* skip_if = nullptr) {
     if (n_parts < 0 || (n_parts > 0 && !parts)) return fail("bad partial sums");
     int rc = ensure_bias_table(o);
     if (rc != SOAR_OK) return rc;
-    const soarb::ApplyArgs a = apply_args(o, parts, n_parts);
+    soarb::ApplyArgs a = apply_args(o, parts, n_parts);
+    a.skip_if = skip_if;
     SOAR_CUDA_TRY(soarb::launch_apply(o.mixed, o.chunks, o.n_chunks, o.n_vec, o.ctl, a,
                                       o.grid_apply, s, ag, o.ema != nullptr, o.sgd));
     o.host_calls += 1;
@@ -485,10 +486,10 @@ void record_error(const std::string& msg) { g_last_error = msg; }
 
 // The update with the fused data-parallel all-gather (zero1.cu).
 int optim_apply_allgather(void* optim, const double* parts, int n_parts, cudaStream_t stream,
-                          const AgArgs& ag) {
+                          const AgArgs& ag, const int* skip_if) {
     Optim& o = *as_optim(optim);
     DeviceGuard g(o.device);
-    return apply_impl(o, parts, n_parts, stream, &ag);
+    return apply_impl(o, parts, n_parts, stream, &ag, skip_if);
 }
 
 // Tensor `index`'s param/grad/numel and the optimizer's layout, control block

@@ -296,7 +296,9 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
         // only read here and only written by the last CTA below.
         int skip = 0, found = 0;
         float norm = 0.0f, coef = a.pending_coef;
-        if (a.n_parts > 0) {
+        if (a.skip_if && *a.skip_if) {
+            skip = 1;  // a peer failed to synchronise: no update (the error flag tells)
+        } else if (a.n_parts > 0) {
             double s = 0.0;
             for (int p = 0; p < a.n_parts; ++p) s += a.parts[p];
             found = !isfinite(s);
@@ -553,6 +555,18 @@ __global__ void k_wait_selftest(uint64_t limit_ns, int* out_error, unsigned long
     }
 }
 
+struct SignalPtrs {
+    Signals* q[kMaxRanks];
+};
+
+__global__ void k_step_done(SignalPtrs sig, int world, int rank, uint64_t epoch, int* err) {
+    if (threadIdx.x != 0) return;
+    // this rank's peer parameter stores finished with the previous kernel
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (int q = 0; q < world; ++q) st_release_sys(&sig.q[q]->done[rank], epoch);
+    wait_flags(sig.q[rank]->done, world, epoch, err);
+}
+
 __global__ void k_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float scale,
                                int32_t tracker) {
     ctl->t = t;
@@ -659,6 +673,14 @@ cudaError_t launch_f32_to_bf16(const float* src, uint16_t* dst, uint64_t n,
 cudaError_t launch_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float scale,
                                 int32_t tracker, cudaStream_t stream) {
     k_set_counters<<<1, 1, 0, stream>>>(ctl, t, skipped, scale, tracker);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_step_done(Signals* const* sig, int world, int rank, uint64_t epoch, int* err,
+                             cudaStream_t stream) {
+    SignalPtrs p{};
+    for (int q = 0; q < world && q < kMaxRanks; ++q) p.q[q] = sig[q];
+    k_step_done<<<1, 32, 0, stream>>>(p, world, rank, epoch, err);
     return cudaGetLastError();
 }
 

@@ -68,6 +68,7 @@ struct ApplyArgs {
     int32_t use_scaler;
     int32_t n_parts;      // number of fp64 partial sums in `parts` (0: no norm info)
     const double* parts;  // device, n_parts partial sums (rank order)
+    const int* skip_if;   // device word or nullptr: nonzero skips the step (failed peer sync)
     const float2* bc;     // device table, bc[t] = (1 - beta1^t, sqrt(1 - beta2^t)), t >= 1
     uint32_t bc_len;      // entries in bc; t >= bc_len uses bc[bc_len - 1]
     // fused weight EMA (ModelEMA::update): shadow = decay*shadow + (1-decay)*weight
@@ -85,6 +86,18 @@ struct ApplyArgs {
 // buffers are symmetric: every rank's flat parameter buffer holds the whole
 // model at identical offsets.
 constexpr int kMaxRanks = 8;
+
+// Per-rank signal block in symmetric (IPC) memory for device-side step
+// synchronisation. Every field is written only by the rank it is indexed by
+// (system-scope release stores into each peer's block) and polled in the
+// local block (acquire loads); values are step epochs, so they only grow.
+struct __align__(256) Signals {
+    uint64_t ready[kMaxRanks];      // ready[q] >= e: rank q's step-e gradients are complete
+    uint64_t part_flag[kMaxRanks];  // part_flag[q] >= e: parts[q] holds rank q's step-e partial
+    double parts[kMaxRanks];        // rank q's sum of squares
+    uint64_t done[kMaxRanks];       // done[q] >= e: rank q's step-e param writes here landed
+};
+
 struct AgArgs {
     int world;
     int rank;
@@ -133,6 +146,10 @@ cudaError_t launch_f32_to_bf16(const float* src, uint16_t* dst, uint64_t n,
 cudaError_t launch_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float scale,
                                 int32_t tracker, cudaStream_t stream);
 
+// Device-synchronised end of a data-parallel step: publishes done[rank] =
+// epoch into every peer's signal block, then waits (bounded) for every rank's.
+cudaError_t launch_step_done(Signals* const* sig, int world, int rank, uint64_t epoch, int* err,
+                             cudaStream_t stream);
 cudaError_t launch_wait_selftest(uint64_t limit_ns, int* out_error, unsigned long long* out_ns,
                                  cudaStream_t stream);
 

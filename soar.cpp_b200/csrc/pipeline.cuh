@@ -97,6 +97,41 @@ __device__ __forceinline__ void bulk_wait_read_all() {
 }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// System-scope release store / acquire load (peer flags over NVLink).
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_sys_f64(double* p, double v) {
+    asm volatile("st.relaxed.sys.global.f64 [%0], %1;" ::"l"(p), "d"(v) : "memory");
+}
+__device__ __forceinline__ double ld_relaxed_sys_f64(const double* p) {
+    double v;
+    asm volatile("ld.relaxed.sys.global.f64 %0, [%1];" : "=d"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded wait until flags[q] >= epoch for every q < n (local memory written
+// by peers). Returns false, setting *err, after limit_ns.
+__device__ __forceinline__ bool wait_flags(const uint64_t* flags, int n, uint64_t epoch, int* err,
+                                           uint64_t limit_ns = kWaitLimitNs) {
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; ++i) {
+        bool all = true;
+        for (int q = 0; q < n; ++q) all = all && (ld_acquire_sys(flags + q) >= epoch);
+        if (all) return true;
+        if (i == 0) t0 = global_timer_ns();
+        if ((i & 255u) == 255u && global_timer_ns() - t0 > limit_ns) {
+            atomicOr(err, 1);
+            return false;
+        }
+    }
+}
+
 // Named barrier 1 over the kThreadsN consumer threads only.
 template <int kThreadsN>
 __device__ __forceinline__ void consumers_sync() {

@@ -16,16 +16,31 @@
 //                buffer in place (bulk store) and accumulate the fp64 sum of
 //                squares of the unscaled result. Each remote tile crosses
 //                NVLink once.
-//   (1-element all-gather of the R partial sums, NCCL, by the caller)
+//   (1-element all-gather of the R partial sums)
 //   k_apply<ag>  the fused update of the owned slices (optim_kernels.cu), whose
 //                bulk stores also write each updated bf16 param tile into every
 //                peer's parameter buffer: the all-gather.
 //
-// Ordering across GPUs is by stream order plus small collectives issued by the
-// caller: a barrier before k_rs_sumsq (all gradients written), the partial-sum
-// all-gather after it (every rank done reading peer gradients), and a barrier
-// after the update (every peer's parameter writes landed). No kernel here waits
-// on another GPU.
+// Ordering across GPUs takes three synchronisation points: before k_rs_sumsq
+// (every rank's gradients are complete), after it (every rank is done reading
+// peer gradients; the partial sums are exchanged) and after the update (every
+// peer's parameter writes landed). Two ways to provide them:
+//   * caller-synchronised (soar_zero1_reduce_sumsq / soar_zero1_apply_allgather):
+//     small collectives issued by the caller between the launches; no kernel
+//     waits on another GPU.
+//   * device-synchronised (soar_zero1_set_signals + soar_zero1_step): epoch
+//     flags in a per-rank signal block of symmetric memory. Every CTA of
+//     k_rs_sumsq publishes ready[rank] = epoch into every peer's block
+//     (system-scope release stores) and waits for all ready flags in its own
+//     block; its last CTA writes the rank's partial into every peer's
+//     parts[rank], then part_flag[rank], waits for all part flags and leaves
+//     the R partials, in rank order, where k_apply reads them. After k_apply
+//     (whose peer stores are complete and fenced when it exits) a one-thread
+//     kernel publishes done[rank] and waits for all done flags. Every wait
+//     polls local memory, is bounded (1 s, then the handle's error flag is set
+//     and the update skips the step) and waits only on flags that are
+//     published before the publisher itself waits, so no wait depends on
+//     co-residency and none can form a cycle.
 #include <algorithm>
 #include <cstring>
 #include <string>
@@ -40,7 +55,7 @@
 namespace soarb {
 void record_error(const std::string& msg);  // optim_capi.cu
 int optim_apply_allgather(void* optim, const double* parts, int n_parts, cudaStream_t stream,
-                          const AgArgs& ag);
+                          const AgArgs& ag, const int* skip_if);
 bool optim_tensor_info(void* optim, int index, void** param, void** grad, uint64_t* numel,
                        bool* mixed, Ctl** ctl, int* device);
 }  // namespace soarb
@@ -84,6 +99,10 @@ struct __align__(16) RsChunk {
 };
 
 struct RsArgs {
+    Signals* sig[kMaxRanks];         // device-synchronised step (nullptr: caller-synchronised)
+    uint64_t epoch;
+    double* parts_out;               // (device sync) the R partials in rank order, for k_apply
+    int* abort_out;                  // (device sync) 1: the step must be skipped
     const uint16_t* src[kMaxRanks];  // every rank's flat gradient buffer
     uint16_t* dst;                   // this rank's flat gradient buffer (reduced in place)
     int world;
@@ -130,7 +149,7 @@ k_rs_sumsq(const RsChunk* __restrict__ chunks, int n_chunks, int n_vec, RsArgs a
     constexpr int kMaxStages = 8;
     __shared__ __align__(8) uint64_t full_bar[kMaxStages], empty_bar[kMaxStages];
     __shared__ double s_red[32];
-    __shared__ int s_err, s_drain_err, s_last;
+    __shared__ int s_err, s_drain_err, s_last, s_abort;
     __shared__ int s_cfail[2];
     __shared__ uint32_t s_issued;
     constexpr int kConsumers = kRsConsumerWarps * 32;
@@ -141,6 +160,14 @@ k_rs_sumsq(const RsChunk* __restrict__ chunks, int n_chunks, int n_vec, RsArgs a
         s_err = s_drain_err = 0;
         s_cfail[0] = s_cfail[1] = 0;
         s_issued = 0;
+        s_abort = 0;
+        if (a.sig[0]) {
+            // this rank's gradients are complete (stream order): tell every
+            // peer, then wait for every peer's
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
+            for (int q = 0; q < a.world; ++q) st_release_sys(&a.sig[q]->ready[a.rank], a.epoch);
+            if (!wait_flags(a.sig[a.rank]->ready, a.world, a.epoch, err)) s_abort = 1;
+        }
         for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&full_bar[s]), 1);
             mbar_init(smem_u32(&empty_bar[s]), 1);
@@ -160,7 +187,9 @@ k_rs_sumsq(const RsChunk* __restrict__ chunks, int n_chunks, int n_vec, RsArgs a
         }
     };
 
-    if (warp == kRsConsumerWarps) {
+    if (s_abort) {
+        // a peer never arrived: read no peer memory (nothing is reduced)
+    } else if (warp == kRsConsumerWarps) {
         if (lane == 0) {
             for_each_tile([&](const RsChunk& ch, uint32_t t0, uint32_t len, uint32_t q) {
                 const uint32_t s = q % S;
@@ -278,6 +307,21 @@ k_rs_sumsq(const RsChunk* __restrict__ chunks, int n_chunks, int n_vec, RsArgs a
     if (threadIdx.x == 0) {
         *out = all;
         *ticket = 0u;
+        if (a.sig[0]) {
+            // Every CTA is done reading peer gradients: publish the partial
+            // (withheld after a failed wait, so the peers time out and skip),
+            // then collect every rank's.
+            int ok = *static_cast<volatile int*>(err) == 0;
+            if (ok) {
+                for (int q = 0; q < a.world; ++q) st_relaxed_sys_f64(&a.sig[q]->parts[a.rank], all);
+                for (int q = 0; q < a.world; ++q) st_release_sys(&a.sig[q]->part_flag[a.rank], a.epoch);
+                ok = wait_flags(a.sig[a.rank]->part_flag, a.world, a.epoch, err);
+            }
+            if (ok)
+                for (int q = 0; q < a.world; ++q)
+                    a.parts_out[q] = ld_relaxed_sys_f64(&a.sig[a.rank]->parts[q]);
+            *a.abort_out = ok ? 0 : 1;
+        }
     }
 }
 
@@ -295,6 +339,8 @@ struct Zero1 {
     Ctl* ctl = nullptr;
     int grid = 1;
     size_t smem = 0;
+    Signals* sig[kMaxRanks] = {};  // device-synchronised step (soar_zero1_set_signals)
+    uint64_t epoch = 0;
 };
 
 }  // namespace
@@ -312,6 +358,8 @@ using soarb::kRsSmemBudget;
 using soarb::k_rs_sumsq;
 using soarb::optim_tensor_info;
 using soarb::optim_apply_allgather;
+using soarb::Signals;
+using soarb::launch_step_done;
 
 extern "C" {
 
@@ -321,8 +369,14 @@ SOAR_API int soar_ipc_alloc(size_t bytes, int device, void** out_ptr, void* out_
     if (!g.ok) return fail("cannot select device");
     void* p = nullptr;
     Z1_CUDA_TRY(cudaMalloc(&p, bytes));
+    cudaError_t e = cudaMemset(p, 0, bytes);  // zero-filled (signal blocks rely on it)
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return fail(std::string("soar_ipc_alloc: ") + cudaGetErrorString(e));
+    }
     cudaIpcMemHandle_t h;
-    cudaError_t e = cudaIpcGetMemHandle(&h, p);
+    e = cudaIpcGetMemHandle(&h, p);
     if (e != cudaSuccess) {
         cudaFree(p);
         return fail(std::string("cudaIpcGetMemHandle: ") + cudaGetErrorString(e));
@@ -504,7 +558,45 @@ SOAR_API int soar_zero1_apply_allgather(void* handle, const double* d_parts, int
     auto* z = static_cast<Zero1*>(handle);
     DeviceGuard g(z->device);
     return optim_apply_allgather(z->optim, d_parts, n_parts, static_cast<cudaStream_t>(stream),
-                                 z->ag);
+                                 z->ag, nullptr);
+}
+
+SOAR_API int soar_zero1_set_signals(void* handle, void* const* signal_bases) {
+    if (!handle || !signal_bases) return fail("null argument");
+    auto* z = static_cast<Zero1*>(handle);
+    if (z->epoch != 0) return fail("signal blocks are set once, before the first device-synchronised step");
+    for (int q = 0; q < z->world; ++q) {
+        if (!signal_bases[q] || reinterpret_cast<uintptr_t>(signal_bases[q]) % alignof(Signals))
+            return fail("signal block " + std::to_string(q) + " is null or not 256-byte aligned");
+    }
+    static_assert(sizeof(Signals) <= SOAR_ZERO1_SIGNAL_BYTES, "signal block size");
+    for (int q = 0; q < z->world; ++q) z->sig[q] = static_cast<Signals*>(signal_bases[q]);
+    return SOAR_OK;
+}
+
+SOAR_API int soar_zero1_step(void* handle, void* stream) {
+    if (!handle) return fail("null handle");
+    auto* z = static_cast<Zero1*>(handle);
+    if (!z->sig[0]) return fail("soar_zero1_step needs soar_zero1_set_signals");
+    DeviceGuard g(z->device);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const uint64_t epoch = z->epoch + 1;
+    soarb::RsArgs rs = z->rs;
+    for (int q = 0; q < z->world; ++q) rs.sig[q] = z->sig[q];
+    rs.epoch = epoch;
+    // the slack past the per-CTA partials: this rank's partial, the R
+    // partials in rank order, the skip word
+    double* part = z->partials + z->grid;
+    rs.parts_out = part + 1;
+    rs.abort_out = reinterpret_cast<int*>(part + 1 + kMaxRanks);
+    k_rs_sumsq<<<z->grid, kRsThreads, z->smem, s>>>(z->d_chunks, z->n_chunks, z->n_vec, rs,
+                                                    z->ctl, z->partials, z->ticket, z->err, part);
+    Z1_CUDA_TRY(cudaGetLastError());
+    const int rc = optim_apply_allgather(z->optim, rs.parts_out, z->world, s, z->ag, rs.abort_out);
+    if (rc != SOAR_OK) return rc;
+    Z1_CUDA_TRY(launch_step_done(z->sig, z->world, z->rank, epoch, z->err, s));
+    z->epoch = epoch;
+    return SOAR_OK;
 }
 
 SOAR_API int soar_zero1_error(void* handle, int* out_error) {

@@ -53,7 +53,7 @@ def build_synth(force: bool = False) -> Path:
         return SYNTH_LIB
     LIBDIR.mkdir(exist_ok=True)
     cc = "/usr/bin/gcc" if Path("/usr/bin/gcc").exists() else "gcc"
-    tmp = SYNTH_LIB.with_suffix(".so.tmp")
+    tmp = SYNTH_LIB.with_suffix(f".so.tmp{os.getpid()}")  # concurrent builders do not collide
     subprocess.run([cc, "-O2", "-std=c11", "-fopenmp", "-fPIC", "-shared", "-ffp-contract=off",
                     "-o", str(tmp), str(SYNTH_SRC), "-lm"], check=True)
     tmp.replace(SYNTH_LIB)
@@ -64,7 +64,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and not _stale():
         return LIB
     LIBDIR.mkdir(exist_ok=True)
-    tmp = LIB.with_suffix(".so.tmp")
+    tmp = LIB.with_suffix(f".so.tmp{os.getpid()}")  # concurrent builders do not collide
     cmd = [nvcc(), *NVCC_FLAGS, "-I", str(INCLUDE), "-o", str(tmp),
            *[str(CSRC / s) for s in SOURCES]]
     if verbose:

@@ -23,8 +23,11 @@ Two drivers:
   optimizer in the host-logic tests).
 * FusedZeroOneAdamW -- steps 1-2 are one kernel and steps 4-5 are one kernel
   over peer memory (soar_zero1_*): the parameter and gradient buffers are
-  allocated by the library and opened by every rank through CUDA IPC; only the
-  8-byte partial all-gather and two 4-byte barriers go through NCCL.
+  allocated by the library and opened by every rank through CUDA IPC. The
+  ranks synchronise either inside the kernels, through epoch flags in a
+  symmetric signal block (sync="device", no host collective in the step), or
+  through an 8-byte partial all-gather and two 4-byte barriers over NCCL
+  (sync="nccl").
 """
 from __future__ import annotations
 
@@ -186,10 +189,15 @@ class FusedZeroOneAdamW:
     make_optimizer(shard_params, shard_grads) -> soar_b200.AdamW (bf16_mixed).
     init_params (n bf16 values, any device) is copied into `params` before the
     optimizer is created, so its fp32 master weights start from them.
+
+    sync="device" (default) synchronises the ranks inside the kernels through
+    epoch flags in a small symmetric signal block (soar_zero1_step: no host
+    collective in the step); sync="nccl" issues the three synchronisation
+    points as small NCCL collectives between the launches.
     """
 
     def __init__(self, n: int, bucket: int, make_optimizer, group=None, device: int | None = None,
-                 init_params=None):
+                 init_params=None, sync: str = "device"):
         import ctypes as C
 
         import torch
@@ -204,11 +212,17 @@ class FusedZeroOneAdamW:
         self.n = n
         self.buckets = plan_buckets(n, bucket, self.world, self.rank)
         self._local, self._peers, self.zero1 = [], [], None
+        if sync not in ("device", "nccl"):
+            raise ValueError("sync must be 'device' or 'nccl'")
+        self.sync = sync
         bases = {}
-        for name in ("grads", "params"):
+        sizes = {"grads": 2 * n, "params": 2 * n}
+        if sync == "device":
+            sizes["signals"] = _o.ZERO1_SIGNAL_BYTES
+        for name, nbytes in sizes.items():
             ptr = C.c_void_p()
             handle = (C.c_ubyte * _o.IPC_HANDLE_BYTES)()
-            _o._check(self.lib.soar_ipc_alloc(2 * n, self.device, C.byref(ptr), handle),
+            _o._check(self.lib.soar_ipc_alloc(nbytes, self.device, C.byref(ptr), handle),
                       "soar_ipc_alloc")
             self._local.append(ptr.value)
             handles = [None] * self.world
@@ -247,6 +261,9 @@ class FusedZeroOneAdamW:
         _o._check(self.lib.soar_zero1_create(self.opt.handle, self.rank, self.world, gb, pb,
                                              shards, len(mine), C.byref(h)), "soar_zero1_create")
         self.zero1 = h
+        if sync == "device":
+            sb = (C.c_void_p * self.world)(*bases["signals"])
+            _o._check(self.lib.soar_zero1_set_signals(h, sb), "soar_zero1_set_signals")
         self.part = torch.zeros(1, dtype=torch.float64, device=dev)
         self.parts = torch.zeros(self.world, dtype=torch.float64, device=dev)
         self.flag = torch.zeros(1, dtype=torch.float32, device=dev)
@@ -278,6 +295,10 @@ class FusedZeroOneAdamW:
                   "soar_zero1_apply_allgather")
 
     def step(self):
+        if self.sync == "device":
+            from . import optim as _o
+            _o._check(self.lib.soar_zero1_step(self.zero1, self._stream()), "soar_zero1_step")
+            return
         self.barrier()                        # every rank's gradients are complete
         self.reduce()                         # reduce-scatter + sum of squares
         self.update(self.gather_partials())   # update + all-gather

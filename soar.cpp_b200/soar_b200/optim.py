@@ -112,6 +112,8 @@ SIGNATURES: dict[str, tuple] = {
                                     C.POINTER(C.c_void_p)]),
     "soar_zero1_reduce_sumsq": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     "soar_zero1_apply_allgather": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
+    "soar_zero1_set_signals": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "soar_zero1_step": (C.c_int, [C.c_void_p, C.c_void_p]),
     "soar_zero1_error": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
     "soar_zero1_destroy": (C.c_int, [C.c_void_p]),
     "soar_selftest_bounded_wait": (C.c_int, [C.c_uint64, C.c_int, C.POINTER(C.c_int),
@@ -120,6 +122,7 @@ SIGNATURES: dict[str, tuple] = {
 }
 
 IPC_HANDLE_BYTES = 64
+ZERO1_SIGNAL_BYTES = 4096
 
 
 class Zero1Shard(C.Structure):

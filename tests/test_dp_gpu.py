@@ -7,7 +7,9 @@ its own, so parity is taken on what the optimizer received: every step the
 ranks' post-reduce-scatter shards are read back, reassembled, and fed to the
 single-process oracle. Checks: identical params on both ranks, skip /
 loss-scale / step sequences bit-exact, params within 1 bf16 ulp, and the
-reduce-scatter within bf16 rounding of the fp64 mean. Skipped below 2 GPUs."""
+reduce-scatter within bf16 rounding of the fp64 mean. The fused path (both
+synchronisation modes) and its bounded device-side waits are tested below.
+Skipped below 2 GPUs."""
 import datetime
 import os
 import queue
@@ -148,7 +150,7 @@ def test_zero1_two_gpus_nccl(oracle_mod):
     assert diff.max() <= 1
 
 
-def _fused_worker(rank, world, port, q):
+def _fused_worker(rank, world, port, q, sync="nccl"):
     import torch
     import torch.distributed as dist
 
@@ -171,19 +173,24 @@ def _fused_worker(rank, world, port, q):
                                                              growth_interval=2),
                             grads=sg, device=rank)
 
-        fz = dp.FusedZeroOneAdamW(N, BUCKET, make, device=rank, init_params=p0)
+        fz = dp.FusedZeroOneAdamW(N, BUCKET, make, device=rank, init_params=p0, sync=sync)
         scale = 1024.0
         reduced, hist = [], []
+        own = lambda: [fz.grads[b.own_start:b.own_start + b.own_size].view(torch.int16).cpu()
+                       .numpy().view(np.uint16).copy() for b in fz.buckets]
         for t in range(1, STEPS + 1):
             fz.grads.copy_(bf(_grads(rank, t, scale)))
-            fz.barrier()
-            fz.reduce()
-            torch.cuda.synchronize()
-            mine = [fz.grads[b.own_start:b.own_start + b.own_size].view(torch.int16).cpu()
-                    .numpy().view(np.uint16).copy() for b in fz.buckets]
-            reduced.append(mine)
-            fz.update(fz.gather_partials())
-            fz.barrier()
+            if sync == "device":
+                fz.step()  # the reduce leaves the averaged slice in place
+                torch.cuda.synchronize()
+                reduced.append(own())
+            else:
+                fz.barrier()
+                fz.reduce()
+                torch.cuda.synchronize()
+                reduced.append(own())
+                fz.update(fz.gather_partials())
+                fz.barrier()
             info = fz.opt.info()
             scale = info.loss_scale
             hist.append((info.skipped, info.loss_scale, info.step))
@@ -196,11 +203,14 @@ def _fused_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_fused_zero1_two_gpus(oracle_mod):
+@pytest.mark.parametrize("sync", ["nccl", "device"])
+def test_fused_zero1_two_gpus(oracle_mod, sync):
     """The fused path: reduce-scatter inside the norm kernel and all-gather
-    inside the update, over peer memory. Its reduce is defined exactly as the
-    oracle's (fp32 sum in rank order, one rounding), so the reduced shards are
-    checked bit-for-bit; the step against the single-process oracle."""
+    inside the update, over peer memory; the ranks synchronised by small NCCL
+    collectives between the launches or by device-side epoch flags. Its
+    reduce is defined exactly as the oracle's (fp32 sum in rank order, one
+    rounding), so the reduced shards are checked bit-for-bit; the step against
+    the single-process oracle."""
     import torch
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
@@ -211,7 +221,8 @@ def test_fused_zero1_two_gpus(oracle_mod):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, q, sync))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -251,3 +262,84 @@ def test_fused_zero1_two_gpus(oracle_mod):
     assert hist[INF_STEP - 1][0] == 1
     diff = np.abs(res[0][0].astype(np.int32) - p_full.astype(np.int32))
     assert diff.max() <= 1
+
+
+def _absent_peer_worker(rank, world, port, q):
+    """Rank 0 steps; rank 1 is alive but never steps. Rank 0's bounded waits
+    (the ready flags, then the done flags: 1 s each; the partial exchange is
+    skipped once a wait failed) run out, the update is skipped and the error
+    flag is set; nothing waits forever."""
+    import torch
+    import torch.distributed as dist
+
+    import soar_b200 as sb
+    from soar_b200 import dp, synth
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    fz = None
+    try:
+        bf = lambda a: torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).cuda()
+        p0 = bf(synth.to_bf16_bits(synth.normal(synth.seed_of(51), N, 0.02)))
+
+        def make(sp, sg):
+            return sb.AdamW([sb.ParamGroup(sp, 0.01)], layout="bf16_mixed", grads=sg,
+                            device=rank)
+
+        fz = dp.FusedZeroOneAdamW(N, BUCKET, make, device=rank, init_params=p0, sync="device")
+        fz.grads.copy_(bf(_grads(rank, 1, 1.0)))
+        dist.barrier()
+        out = None
+        if rank == 0:
+            before = fz.params.view(torch.int16).cpu().numpy().copy()
+            t0 = time.time()
+            fz.step()
+            torch.cuda.synchronize()
+            waited = time.time() - t0
+            after = fz.params.view(torch.int16).cpu().numpy()
+            info = fz.opt.info()
+            out = (fz.error(), waited, bool((before == after).all()), info.step, info.skipped)
+        dist.barrier()  # rank 1 keeps its buffers mapped until rank 0 is done
+        q.put((rank, out))
+    finally:
+        if fz is not None:
+            fz.close()
+        dist.destroy_process_group()
+
+
+def test_device_sync_wait_times_out_and_reports():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_absent_peer_worker, args=(r, world, port, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    deadline = time.time() + 300
+    while len(res) < world and time.time() < deadline:
+        try:
+            r, out = q.get(timeout=2)
+            res[r] = out
+        except queue.Empty:
+            if any(p.exitcode not in (None, 0) for p in procs):
+                break
+    for p in procs:
+        if p.is_alive() and len(res) < world:
+            p.terminate()
+        p.join(timeout=60)
+    assert len(res) == world, "a rank failed"
+    err, waited, unchanged, step, skipped = res[0]
+    assert err == 1
+    assert 1.5 < waited < 30.0, waited      # two bounded waits of 1 s (ready, then done)
+    assert unchanged                        # the update was skipped
+    assert (step, skipped) == (0, 1)        # and counted as a skipped step
