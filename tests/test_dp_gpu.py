@@ -343,3 +343,131 @@ def test_device_sync_wait_times_out_and_reports():
     assert 1.5 < waited < 30.0, waited      # two bounded waits of 1 s (ready, then done)
     assert unchanged                        # the update was skipped
     assert (step, skipped) == (0, 1)        # and counted as a skipped step
+
+
+N4, B4 = 200_000_000, 25_000_000   # config 4 in full
+
+
+def _full_c4_worker(rank, world, port, q):
+    """Config 4 at full size on 2 GPUs (device-synchronised fused step) against
+    a single-GPU step on the average gradient (the oracle's reduce: fp32 sum in
+    rank order, one multiply by 1/R, one bf16 rounding), on rank 0."""
+    import torch
+    import torch.distributed as dist
+
+    import soar_b200 as sb
+    from soar_b200 import dp
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    fz = ref = None
+    try:
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(4000 + rank)
+        p0 = (torch.randn(N4, device="cuda", generator=gen) * 0.02).bfloat16()
+        dist.broadcast(p0, 0)
+        scaler = sb.LossScalerOptions(init_scale=65536.0)
+
+        def make(sp, sg):
+            return sb.AdamW([sb.ParamGroup(sp, 0.01)], layout="bf16_mixed", max_grad_norm=1.0,
+                            loss_scaler=scaler, grads=sg, device=rank)
+
+        fz = dp.FusedZeroOneAdamW(N4, B4, make, device=rank, init_params=p0, sync="device")
+        full = dp.plan_buckets(N4, B4, 1, 0)
+        if rank == 0:
+            ref_p = p0.clone()
+            ref_g = torch.empty_like(ref_p)
+            ref = make([ref_p[b.start:b.start + b.size] for b in full],
+                       [ref_g[b.start:b.start + b.size] for b in full])
+        scale = 65536.0
+        for t in range(1, 4):
+            fz.grads.copy_((torch.randn(N4, device="cuda", generator=gen) * (1e-3 * scale))
+                           .bfloat16())
+            if t == 2 and rank == 1:
+                fz.grads[123_456_789] = float("inf")
+            if rank == 1:
+                dist.send(fz.grads.clone(), 0)
+            else:
+                other = torch.empty_like(fz.grads)
+                dist.recv(other, 1)
+                ref_g.copy_(((fz.grads.float() + other.float()) * 0.5).bfloat16())
+                del other
+            fz.step()
+            if ref is not None:
+                ref.step()
+            scale = fz.opt.info().loss_scale
+        torch.cuda.synchronize()
+        i = fz.opt.info()
+        out = {"info": (i.step, i.skipped, i.loss_scale), "err": fz.error()}
+        if rank == 1:
+            dist.send(fz.params.clone(), 0)
+        else:
+            other = torch.empty_like(fz.params)
+            dist.recv(other, 1)
+            out["ranks_equal"] = bool(torch.equal(other.view(torch.int16),
+                                                  fz.params.view(torch.int16)))
+            del other
+
+            def ordered(x):
+                x = x.view(torch.int16).int()
+                return torch.where(x < 0, -(x & 0x7FFF), x)
+            d = (ordered(fz.params) - ordered(ref_p)).abs()
+            out["max_ulp"] = int(d.max())
+            out["ulp_mismatches"] = int((d > 0).sum())
+            ri = ref.info()
+            out["ref_info"] = (ri.step, ri.skipped, ri.loss_scale)
+            worst = 0.0
+            mine = [b for b in fz.buckets if b.own_size > 0]
+            for k, b in enumerate(mine):
+                lo = b.own_start - full[b.index].start
+                for kind in (sb.STATE_MASTER, sb.STATE_M, sb.STATE_V):
+                    a = fz.opt.state(k, kind).double()
+                    r = ref.state(b.index, kind)[lo:lo + b.own_size].double()
+                    den = r.abs().clamp_min(1e-30)
+                    worst = max(worst, float(((a - r).abs() / den).max()))
+            out["state_max_rel"] = worst
+        q.put((rank, out))
+    finally:
+        if ref is not None:
+            ref.close()
+        if fz is not None:
+            fz.close()
+        dist.destroy_process_group()
+
+
+def test_config4_full_size_two_gpus():
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_full_c4_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    deadline = time.time() + 400
+    while len(res) < world and time.time() < deadline:
+        try:
+            r, out = q.get(timeout=2)
+            res[r] = out
+        except queue.Empty:
+            if any(p.exitcode not in (None, 0) for p in procs):
+                break
+    for p in procs:
+        if p.is_alive() and len(res) < world:
+            p.terminate()
+        p.join(timeout=60)
+    assert len(res) == world, "a rank failed"
+    r0 = res[0]
+    print("CONFIG4_FULL_DP2", r0)
+    assert r0["err"] == 0 and res[1]["err"] == 0
+    assert r0["info"] == res[1]["info"] == r0["ref_info"] == (2, 1, 32768.0)
+    assert r0["ranks_equal"]
+    assert r0["max_ulp"] <= 1
+    assert r0["state_max_rel"] <= 1e-6
