@@ -319,6 +319,7 @@ def run_ours(args):
     if comm:
         torch.distributed.all_reduce(ph, op=torch.distributed.ReduceOp.MAX)
     phases = {k: round(float(v), 4) for k, v in zip(phase_names, ph.tolist())}
+    nvl = nvlink_rates(torch, world, rank, local, 2 * shard_params, phases) if fused else None
     if apply_ms is None:  # device-synchronised step: the update phase of the loop above
         apply_ms = [float(ph[phase_names.index("update+allgather")])]
     t = torch.tensor([ms, statistics.mean(apply_ms)], dtype=torch.float64, device=dev)
@@ -402,11 +403,90 @@ def run_ours(args):
         "clocks": clock_info,
         "gpu_launches": launches_per_step * args.steps,
         "phases_ms": phases,
+        "nvlink": nvl,
         "final_info": {"step": info.step, "skipped": info.skipped, "loss_scale": info.loss_scale,
                        "grad_norm": info.grad_norm},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def nvlink_rates(torch, world, rank, local, shard_bytes, phases):
+    """The fused kernels' NVLink rates against the raw rates of their access
+    patterns on this box (soar_nvlink_probe: all ranks at once, no arithmetic,
+    the same bytes per peer as the step). GB/s per direction per rank; max
+    time over ranks."""
+    import ctypes as C
+
+    import torch.distributed as dist
+
+    from soar_b200 import optim as _o
+    lib = _o.lib()
+    tile_lcm = 64 * 1024
+    bpp = max(tile_lcm, shard_bytes // tile_lcm * tile_lcm)
+    ptr = C.c_void_p()
+    handle = (C.c_ubyte * _o.IPC_HANDLE_BYTES)()
+    _o._check(lib.soar_ipc_alloc(world * bpp, local, C.byref(ptr), handle), "soar_ipc_alloc")
+    handles = [None] * world
+    dist.all_gather_object(handles, bytes(handle))
+    bases, opened = [], []
+    for q, h in enumerate(handles):
+        if q == rank:
+            bases.append(ptr.value)
+            continue
+        peer = C.c_void_p()
+        buf = (C.c_ubyte * _o.IPC_HANDLE_BYTES).from_buffer_copy(h)
+        _o._check(lib.soar_ipc_open(buf, local, C.byref(peer)), "soar_ipc_open")
+        bases.append(peer.value)
+        opened.append(peer.value)
+    arr = (C.c_void_p * world)(*bases)
+    err = torch.zeros(1, dtype=torch.int32, device=f"cuda:{local}")
+    stream = torch.cuda.current_stream()
+    sms = torch.cuda.get_device_properties(local).multi_processor_count
+    gbs = lambda ms: (world - 1) * bpp / (ms * 1e-3) / 1e9
+
+    def timed(mode, tile, stages, grid, reps=5):
+        def launch():
+            _o._check(lib.soar_nvlink_probe(arr, world, rank, bpp, mode, tile, stages, grid,
+                                            C.c_void_p(err.data_ptr()),
+                                            C.c_void_p(stream.cuda_stream)), "soar_nvlink_probe")
+        for _ in range(2):
+            launch()
+        torch.cuda.synchronize()
+        dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            launch()
+        b.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b) / reps], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return round(gbs(float(t[0])), 1)
+
+    pull = {f"tile{tile}_stages{st}_grid{g}": timed(0, tile, st, g)
+            for tile, st, g in ((4096, 4, sms), (2048, 8, 2 * sms))
+            if st * tile * (world - 1) <= 200 * 1024}
+    push = {f"tile{tile}_grid{g}": timed(1, tile, 0, g)
+            for tile, g in ((2048, 2 * sms), (8192, sms))}
+    torch.cuda.synchronize()
+    failed = int(err.item())
+    dist.barrier(device_ids=[local])
+    for pp in opened:
+        lib.soar_ipc_close(C.c_void_p(pp), local)
+    dist.barrier(device_ids=[local])
+    lib.soar_ipc_free(ptr, local)
+    rs = (world - 1) * shard_bytes / (phases["reduce_scatter+sumsq"] * 1e-3) / 1e9
+    ag = (world - 1) * shard_bytes / (phases["update+allgather"] * 1e-3) / 1e9
+    p_pull, p_push = max(pull.values()), max(push.values())
+    return {"unit": "GB/s per direction per rank", "bytes_per_peer": shard_bytes,
+            "k_rs_sumsq": {"achieved": round(rs, 1), "peak": p_pull, "frac": round(rs / p_pull, 3),
+                           "peak_kind": "measured: soar_nvlink_probe pull, all ranks at once"},
+            "k_apply_allgather": {"achieved": round(ag, 1), "peak": p_push,
+                                  "frac": round(ag / p_push, 3),
+                                  "peak_kind": "measured: soar_nvlink_probe push, all ranks at once"},
+            "probe": {"pull": pull, "push": push, "wait_error": failed}}
 
 
 def run_sweep(args):

@@ -303,6 +303,21 @@ SOAR_API int soar_zero1_set_signals(void* zero1_handle, void* const* signal_base
    checkpoint. */
 SOAR_API int soar_zero1_step(void* zero1_handle, void* stream);
 
+/* Measurement, no reference counterpart: the raw NVLink rate of the fused
+   step's two peer-memory access patterns, with no arithmetic, on symmetric
+   buffers of at least world * bytes_per_peer bytes (bases[q]: rank q's, as
+   seen from this process; 16-byte aligned). Every rank calls it at once.
+   mode 0 (pull, k_rs_sumsq's reads): bulk-loads bytes [rank * bytes_per_peer,
+   (rank + 1) * bytes_per_peer) of every peer's buffer into a shared-memory
+   ring of `stages` stages of tile_bytes per peer (stages * tile_bytes *
+   (world - 1) <= 200 KB). mode 1 (push, k_apply's all-gather writes):
+   bulk-stores zero tiles into that range of every peer's buffer (overwrites
+   it). tile_bytes: a multiple of 16 dividing bytes_per_peer. `grid` CTAs.
+   A wait that runs out (1 s) sets *d_err. */
+SOAR_API int soar_nvlink_probe(void* const* bases, int world, int rank, uint64_t bytes_per_peer,
+                               int mode, uint32_t tile_bytes, int stages, int grid, int* d_err,
+                               void* stream);
+
 /* Nonzero in *out_error if a device-side wait of the data-parallel step timed
    out (synchronises the device). */
 SOAR_API int soar_zero1_error(void* zero1_handle, int* out_error);

@@ -14,7 +14,7 @@ LIBDIR = ROOT / "lib"
 LIB = LIBDIR / "libsoar_optim.so"
 INCLUDE = ROOT.parent / "include"
 
-SOURCES = ["optim_kernels.cu", "optim_capi.cu", "noalloc_sumsq.cu", "zero1.cu"]
+SOURCES = ["optim_kernels.cu", "optim_capi.cu", "noalloc_sumsq.cu", "zero1.cu", "nvlink_probe.cu"]
 HEADERS = ["optim_kernels.cuh", "pipeline.cuh"]
 
 NVCC_FLAGS = [

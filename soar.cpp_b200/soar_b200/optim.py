@@ -115,6 +115,8 @@ SIGNATURES: dict[str, tuple] = {
     "soar_zero1_set_signals": (C.c_int, [C.c_void_p, C.c_void_p]),
     "soar_zero1_step": (C.c_int, [C.c_void_p, C.c_void_p]),
     "soar_zero1_error": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "soar_nvlink_probe": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_uint64, C.c_int,
+                                    C.c_uint32, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "soar_zero1_destroy": (C.c_int, [C.c_void_p]),
     "soar_selftest_bounded_wait": (C.c_int, [C.c_uint64, C.c_int, C.POINTER(C.c_int),
                                              C.POINTER(C.c_uint64)]),
