@@ -159,7 +159,14 @@ SOAR_API int soar_optim_destroy(void* handle);
    the clip_grad_norm() call before it (adamw.cpp:87-117) -- as one fused
    device step: unscale, inf/NaN detect, global norm, clip, AdamW with
    per-tensor wd on the fp32 master, bf16 write-back, loss-scale update.
-   Enqueued on `stream`; never synchronises the host. */
+   Enqueued on `stream`; never synchronises the host. It may be captured into
+   a CUDA graph (stream capture on `stream`): the step count, loss scale and
+   skip decision live on the device, so every replay is a correct next step;
+   the lr (and a pending standalone clip coefficient) are taken at capture,
+   so a changed lr needs a new capture. (With beta2 so close to 1 that
+   1 - beta2^t stays below 1.0f for more than 61440 steps, the
+   bias-correction table grows on the host at those steps; such a step is not
+   capture-safe.) */
 SOAR_API int soar_optim_step(void* handle, void* stream);
 
 /* Replaces AdamW::clip_grad_norm(max_norm) (adamw.cpp:87-117): returns the
