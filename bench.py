@@ -496,31 +496,62 @@ def run_sweep(args):
     back on one stream. Prints one JSON line per (layout, N): Gparams/s and
     k_apply's achieved GB/s at 28 B/param against the measured HBM peak, and
     the same K steps replayed from a CUDA graph (`graph`: device time, without
-    the per-step host launch cost that dominates below ~4M params). Single GPU."""
+    the per-step host launch cost that dominates below ~4M params). Under
+    torchrun every rank runs the same sweep on its own GPU as an independent
+    replica (the update has no cross-GPU term without a reduce): the ranks
+    start each timed region together and the time is the max over ranks;
+    `value` counts all ranks' params."""
     import torch
 
     import soar_b200 as sb
-    torch.cuda.set_device(0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    def sync_max(x):
+        """Barrier-free max over ranks of a host float (one tiny all-reduce)."""
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t[0])
+
+    def together():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier(device_ids=[local])
+            torch.cuda.synchronize()
+
     peak, peak_kind = measured_peak_hbm()
-    free = torch.cuda.mem_get_info()[0]
+    free = sync_max(-torch.cuda.mem_get_info()[0]) * -1  # the smallest free memory of any rank
     for layout in ("fp32", "bf16_mixed"):
         for n in [int(x) for x in args.sweep_sizes.split(",")]:
             need = 16 * n + (12 * n if layout == "bf16_mixed" else 8 * n)
             if need > 0.9 * free:
-                print(json.dumps({"sweep": True, "layout": layout, "params": n,
-                                  "skipped": f"needs {need / 1e9:.1f} GB"}), flush=True)
+                if rank == 0:
+                    print(json.dumps({"sweep": True, "layout": layout, "params": n,
+                                      "skipped": f"needs {need / 1e9:.1f} GB"}), flush=True)
                 continue
             dt = torch.bfloat16 if layout == "bf16_mixed" else torch.float32
             p = (torch.randn(n, device="cuda") * 0.02).to(dt)
             g = (torch.randn(n, device="cuda") * 1e-3).to(dt)
             opt = sb.AdamW([p], sb.AdamWOptions(lr=1e-3, weight_decay=0.01), layout=layout,
-                           grads=[g])
+                           grads=[g], device=local)
             s = torch.cuda.Stream()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             with torch.cuda.stream(s):
                 for _ in range(3):
                     opt.step(s)
-                torch.cuda.synchronize()
+            together()
+            with torch.cuda.stream(s):
                 # K steps back to back through the API (host launch overhead included
                 # wherever it exceeds a step's device time)
                 a.record(s)
@@ -528,7 +559,7 @@ def run_sweep(args):
                     opt.step(s)
                 b.record(s)
             torch.cuda.synchronize()
-            ms = a.elapsed_time(b) / args.steps
+            ms = sync_max(a.elapsed_time(b) / args.steps)
             # the same K steps captured once in a CUDA graph and replayed: device time
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=s):
@@ -536,27 +567,34 @@ def run_sweep(args):
                     opt.step(s)
             with torch.cuda.stream(s):
                 graph.replay()
-                torch.cuda.synchronize()
+            together()
+            with torch.cuda.stream(s):
                 a.record(s)
                 graph.replay()
                 b.record(s)
             torch.cuda.synchronize()
-            gms = a.elapsed_time(b) / args.steps
+            gms = sync_max(a.elapsed_time(b) / args.steps)
             del graph
             gbs = BYTES_PER_PARAM * n / (ms * 1e-3) / 1e9
             ggbs = BYTES_PER_PARAM * n / (gms * 1e-3) / 1e9
-            print(json.dumps({"sweep": True, "metric": "AdamW Gparams/s (config 5 sweep)",
-                              "layout": layout, "params": n, "steps": args.steps, "warmup": 3,
-                              "ms_per_step": ms, "value": n / (ms * 1e-3) / 1e9,
-                              "unit": "Gparams/s", "achieved_gbs": gbs, "peak_gbs": peak,
-                              "peak_kind": peak_kind, "frac": gbs / peak,
-                              "graph": {"ms_per_step": gms, "value": n / (gms * 1e-3) / 1e9,
-                                        "achieved_gbs": ggbs, "frac": ggbs / peak},
-                              "l2": "larger than L2" if 16 * n > 126e6 else "fits in L2"}),
-                  flush=True)
+            if rank == 0:
+                print(json.dumps({"sweep": True, "metric": "AdamW Gparams/s (config 5 sweep)",
+                                  "layout": layout, "params": n, "n_gpus": world,
+                                  "scaling": "weak", "steps": args.steps, "warmup": 3,
+                                  "ms_per_step": ms, "value": world * n / (ms * 1e-3) / 1e9,
+                                  "unit": "Gparams/s", "achieved_gbs_per_gpu": gbs,
+                                  "peak_gbs": peak, "peak_kind": peak_kind, "frac": gbs / peak,
+                                  "graph": {"ms_per_step": gms,
+                                            "value": world * n / (gms * 1e-3) / 1e9,
+                                            "achieved_gbs_per_gpu": ggbs, "frac": ggbs / peak},
+                                  "l2": "larger than L2" if 16 * n > 126e6 else "fits in L2"}),
+                      flush=True)
             opt.close()
             del p, g, opt
             torch.cuda.empty_cache()
+    if dist is not None:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
     return 0
 
 
