@@ -64,3 +64,26 @@ def test_null_arguments_return_error():
     assert lib.soar_cosine_step(None) == -1
     out = ctypes.c_void_p()
     assert lib.soar_optim_create(None, 1, None, ctypes.byref(out)) == -1
+
+
+def test_data_parallel_entry_points_reject_bad_arguments():
+    """Argument checks that run before any CUDA call (no GPU needed)."""
+    lib = sb.lib()
+    assert lib.soar_zero1_step(None, None) == -1
+    assert b"null" in lib.soar_last_error()
+    assert lib.soar_zero1_set_signals(None, None) == -1
+    assert lib.soar_zero1_error(None, None) == -1
+    err = ctypes.c_int()
+    bases = (ctypes.c_void_p * 2)(16, 32)
+    # world must be 2..8, rank inside it, mode 0 or 1
+    assert lib.soar_nvlink_probe(bases, 1, 0, 1 << 20, 0, 4096, 2, 1, ctypes.byref(err), None) == -1
+    assert lib.soar_nvlink_probe(bases, 2, 2, 1 << 20, 0, 4096, 2, 1, ctypes.byref(err), None) == -1
+    assert lib.soar_nvlink_probe(bases, 2, 0, 1 << 20, 2, 4096, 2, 1, ctypes.byref(err), None) == -1
+    # tiles: multiples of 16 that divide the per-peer bytes
+    assert lib.soar_nvlink_probe(bases, 2, 0, 1 << 20, 1, 4000, 0, 1, ctypes.byref(err), None) == -1
+    assert b"tile" in lib.soar_last_error()
+    assert lib.soar_nvlink_probe(bases, 2, 0, 1000, 1, 4096, 0, 1, ctypes.byref(err), None) == -1
+    # the pull ring must fit: stages x tile x (world - 1) <= 200 KB
+    big = (ctypes.c_void_p * 8)(*[16 * (i + 1) for i in range(8)])
+    assert lib.soar_nvlink_probe(big, 8, 0, 1 << 20, 0, 16384, 2, 1, ctypes.byref(err), None) == -1
+    assert b"ring" in lib.soar_last_error()
