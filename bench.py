@@ -139,24 +139,102 @@ def run_reference(args):
 # ------------------------------------------------------------------ clocks --
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clocks and clock-event reasons of the GPUs in use, sampled during the
+    timed region (reads only; no setting is touched). An NVML thread samples
+    every ~5 ms, so even a timed region of a few tens of ms gets several
+    samples; without NVML, `nvidia-smi -lms 200` into a temporary file."""
 
-    def __init__(self, path: Path):
-        self.path = path
-        self.proc = None
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+    FIELDS = ("index,clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, devices: list[int]):
+        self.devices = devices
+        self.samples = []          # (time, device position, sm MHz, reason names)
+        self.max_mhz = []
+        self.window = [None, None]
+        self.thread = self.proc = None
+        self.stopping = False
+
+    def _nvml_handles(self, nvml):
+        import torch
+        out = []
+        for d in self.devices:
+            p = torch.cuda.get_device_properties(d)
+            for i in range(nvml.nvmlDeviceGetCount()):
+                h = nvml.nvmlDeviceGetHandleByIndex(i)
+                pci = nvml.nvmlDeviceGetPciInfo(h)
+                if (pci.domain, pci.bus, pci.device) == (p.pci_domain_id, p.pci_bus_id,
+                                                          p.pci_device_id):
+                    out.append(h)
+                    break
+            else:
+                raise RuntimeError("no NVML device for cuda:%d" % d)
+        return out
 
     def start(self):
+        import threading
         try:
-            self.fh = open(self.path, "w")
+            import pynvml as nvml
+            nvml.nvmlInit()
+            handles = self._nvml_handles(nvml)
+            self.max_mhz = [nvml.nvmlDeviceGetMaxClockInfo(h, nvml.NVML_CLOCK_SM) for h in handles]
+            masks = [(name, getattr(nvml, const)) for name, const in self.REASONS]
+
+            def run():
+                while not self.stopping:
+                    t = time.perf_counter()
+                    for k, h in enumerate(handles):
+                        try:
+                            sm = nvml.nvmlDeviceGetClockInfo(h, nvml.NVML_CLOCK_SM)
+                            r = nvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        except Exception:
+                            continue
+                        self.samples.append((t, k, float(sm), [n for n, m in masks if r & m]))
+                    time.sleep(0.005)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.thread = None
+            self._start_smi()
+
+    def _start_smi(self):
+        import tempfile
+        try:
+            self.fh = tempfile.NamedTemporaryFile("w+", suffix=".csv")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
 
-    def stop(self, gpus: list[int]) -> dict | None:
+    def begin(self):
+        self.window[0] = time.perf_counter()
+
+    def end(self):
+        self.window[1] = time.perf_counter()
+
+    def stop(self) -> dict | None:
+        if self.thread is not None:
+            self.stopping = True
+            self.thread.join(5)
+            lo, hi = self.window
+            inside = [x for x in self.samples if lo is not None and hi is not None and
+                      lo - 0.005 <= x[0] <= hi + 0.005]
+            if not inside and self.samples and hi is not None:   # the nearest sample after the end
+                after = [x for x in self.samples if x[0] >= hi]
+                inside = after[:len(self.devices)] or self.samples[-len(self.devices):]
+            if not inside:
+                return None
+            reasons = sorted({n for x in inside for n in x[3]})
+            return {"sm_mhz": statistics.median(x[2] for x in inside),
+                    "sm_max_mhz": max(self.max_mhz), "reasons": reasons,
+                    "samples": len(inside), "source": "nvml"}
         if not self.proc:
             return None
         self.proc.terminate()
@@ -164,25 +242,26 @@ class ClockSampler:
             self.proc.wait(5)
         except Exception:
             self.proc.kill()
-        self.fh.close()
+        self.fh.seek(0)
         sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.path.read_text().splitlines():
+        names = [n for n, _ in self.REASONS]
+        for line in self.fh.read().splitlines():
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 9 or not f[0].isdigit() or int(f[0]) not in gpus:
+            if len(f) < 7 or not f[0].isdigit() or int(f[0]) not in self.devices:
                 continue
             try:
                 sm.append(float(f[1]))
                 mx.append(float(f[2]))
             except ValueError:
                 continue
-            for nm, v in zip(names, f[5:9]):
+            for nm, v in zip(names, f[3:7]):
                 if v.lower() == "active":
                     reasons.add(nm)
+        self.fh.close()
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx),
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi"}
 
 
 # ----------------------------------------------------------------- our arm --
@@ -266,10 +345,9 @@ def run_ours(args):
     for _ in range(args.warmup):
         one_step()
     # the clock sampler starts before the barrier, so no rank enters the timed
-    # region while another is still setting it up
-    clocks = ClockSampler(ROOT / "gpurun_out" / f"clocks_rank{rank}.csv") if rank == 0 else None
+    # region while another is still setting it up; rank 0 samples every GPU
+    clocks = ClockSampler(list(range(world))) if rank == 0 else None
     if clocks:
-        (ROOT / "gpurun_out").mkdir(exist_ok=True)
         clocks.start()
         time.sleep(0.3)
     torch.cuda.synchronize()
@@ -278,14 +356,18 @@ def run_ours(args):
     apply_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                 for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if clocks:
+        clocks.begin()
     start.record(stream)
     for k in range(args.steps):
         one_step(apply_ev[k])
     end.record(stream)
     torch.cuda.synchronize()
+    if clocks:
+        clocks.end()   # the device work of the timed region is done here
     barrier()
     torch.cuda.synchronize()
-    clock_info = clocks.stop(list(range(world))) if clocks else None
+    clock_info = clocks.stop() if clocks else None
 
     ms = start.elapsed_time(end)
     apply_ms = None if dev_sync else [a.elapsed_time(b) for a, b in apply_ev]

@@ -10,7 +10,7 @@
 //                 shuffle, block, then a single-pass grid reduction (each CTA
 //                 writes its partial, the last CTA to take a ticket folds them
 //                 in fixed order). Non-finite gradients make the sum
-//                 non-finite, so the same number carries the inf/NaN verdict.
+//                 non-finite, so the same number carries the inf/NaN flag.
 //   k_apply       derives skip / clip coefficient / bias corrections from the
 //                 partial sums, then streams the update through a shared-memory
 //                 pipeline: one producer thread issues 1D bulk async copies
