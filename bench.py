@@ -67,6 +67,9 @@ def parse():
                     help="config 5: flat 1M..2B params in both layouts, one JSON line each "
                          "(not the headline line)")
     ap.add_argument("--sweep-sizes", default="1000000,16000000,256000000,1000000000,2000000000")
+    ap.add_argument("--configs", action="store_true",
+                    help="configs 1-3 at their own shapes on one GPU, one JSON line each "
+                         "(not the headline line)")
     ap.add_argument("--dp", default="fused", choices=["fused", "fused-nccl", "nccl"],
                     help="N>1: collectives fused into the kernels over peer memory, the ranks "
                          "synchronised by device-side flags (default) or by small NCCL "
@@ -687,12 +690,88 @@ def run_sweep(args):
     return 0
 
 
+def run_configs(args):
+    """BASELINE configs 1-3 at their own shapes on one GPU, K steps back to back
+    through the API after 3 warm-up, one JSON line each: Gparams/s, step ms and
+    k_apply-equivalent GB/s (28 B/param) against the measured HBM copy.
+      c1  1 fp32 tensor of 1,048,576 params, no clip/scaler;
+      c2  the 240-tensor segmentation-net list (~12M fp32), wd 0.05 on conv
+          weights / 0 on norms and biases, cosine 1e-3 -> 1e-5 over 100 steps
+          (the scheduler steps after every step, on the host);
+      c3  400 bf16-mixed tensors summing to 50M, clip 1.0, loss scaler 65536.
+    Inputs are device-generated; the numerics of these configs are pinned by
+    the parity tests, not here."""
+    import math
+
+    import torch
+
+    import soar_b200 as sb
+    from soar_b200 import synth
+    torch.cuda.set_device(0)
+    peak, peak_kind = measured_peak_hbm()
+
+    def rnd(n, std, dt):
+        return (torch.randn(n, device="cuda") * std).to(dt)
+
+    c2_shapes = synth.config2_shapes()
+    cfgs = {
+        "c1": dict(sizes=[1_048_576], wd=[0.01], layout="fp32", clip=0.0, scaler=None,
+                   cosine=None),
+        "c2": dict(sizes=[int(math.prod(sh)) for _, sh in c2_shapes],
+                   wd=[0.05 if k in ("dw", "pw") else 0.0 for k, _ in c2_shapes],
+                   layout="fp32", clip=0.0, scaler=None, cosine=(100, 1e-5, 0)),
+        "c3": dict(sizes=synth.config3_sizes(), wd=None, layout="bf16_mixed", clip=1.0,
+                   scaler=sb.LossScalerOptions(init_scale=65536.0), cosine=None),
+    }
+    for name, c in cfgs.items():
+        dt = torch.bfloat16 if c["layout"] == "bf16_mixed" else torch.float32
+        ps = [rnd(n, 0.02, dt) for n in c["sizes"]]
+        gs = [rnd(n, 1e-3 * (65536.0 if c["scaler"] else 1.0), dt) for n in c["sizes"]]
+        wds = c["wd"] or [0.01] * len(ps)
+        groups = [sb.ParamGroup([p], w) for p, w in zip(ps, wds)]
+        opt = sb.AdamW(groups, sb.AdamWOptions(lr=1e-3), layout=c["layout"],
+                       max_grad_norm=c["clip"], loss_scaler=c["scaler"], grads=gs)
+        sched = sb.CosineAnnealingLR(opt, *c["cosine"]) if c["cosine"] else None
+        s = torch.cuda.Stream()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                opt.step(s)
+            torch.cuda.synchronize()
+            a.record(s)
+            for _ in range(args.steps):
+                opt.step(s)
+                if sched:
+                    sched.step()
+            b.record(s)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / args.steps
+        n = sum(c["sizes"])
+        gbs = BYTES_PER_PARAM * n / (ms * 1e-3) / 1e9
+        info = opt.info()
+        print(json.dumps({"config": name, "metric": "AdamW Gparams/s (BASELINE configs 1-3)",
+                          "params": n, "tensors": len(c["sizes"]), "layout": c["layout"],
+                          "steps": args.steps, "warmup": 3, "ms_per_step": ms,
+                          "value": n / (ms * 1e-3) / 1e9, "unit": "Gparams/s",
+                          "achieved_gbs": gbs, "peak_gbs": peak, "peak_kind": peak_kind,
+                          "frac": gbs / peak, "final_step": info.step,
+                          "skipped": info.skipped}), flush=True)
+        if sched:
+            sched.close()
+        opt.close()
+        del ps, gs, opt
+        torch.cuda.empty_cache()
+    return 0
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
     if args.sweep:
         return run_sweep(args)
+    if args.configs:
+        return run_configs(args)
     return run_ours(args)
 
 
