@@ -198,13 +198,13 @@ __device__ __forceinline__ float prep_grad(float graw, const StepCoeffs& k) {
     return __fmul_rn(__fmul_rn(graw, k.inv), k.coef);
 }
 
-// Elements [from, to) of a chunk, straight from global memory. With kAg the
-// updated params are also written into every peer's parameter buffer.
 // ModelEMA::update (ema.hpp:24) for one weight: decay*shadow + (1-decay)*weight.
 __device__ __forceinline__ float ema_elem(float sh, float w, const ApplyArgs& a) {
     return __fadd_rn(__fmul_rn(a.ema_decay, sh), __fmul_rn(a.ema_omd, w));
 }
 
+// Elements [from, to) of a chunk, straight from global memory. With kAg the
+// updated params are also written into every peer's parameter buffer.
 template <bool kMixed, bool kAg, bool kEma, bool kSgd>
 __device__ __forceinline__ void apply_scalar(const Chunk& ch, uint32_t from, uint32_t to,
                                              uint32_t tid, uint32_t nthreads, const ApplyArgs& a,
