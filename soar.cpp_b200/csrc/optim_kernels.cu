@@ -98,6 +98,8 @@ k_grad_sumsq(const Chunk* __restrict__ chunks, int n_chunks, Ctl* __restrict__ c
              double* __restrict__ partials, int use_scaler, double* __restrict__ out) {
     __shared__ double s_red[32];
     __shared__ int s_last;
+    pdl_wait();
+    pdl_trigger();
     const float inv = use_scaler ? __fdiv_rn(1.0f, ctl->scale) : 1.0f;
     double acc = 0.0;
     for (int c = blockIdx.x; c < n_chunks; c += gridDim.x) {
@@ -291,6 +293,8 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
     constexpr int kConsumers = kConsumerWarps * 32;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
+    pdl_trigger();
     if (threadIdx.x == 0) {
         // Every CTA derives the same decision from the same bits; counters are
         // only read here and only written by the last CTA below.
@@ -560,6 +564,8 @@ struct SignalPtrs {
 };
 
 __global__ void k_step_done(SignalPtrs sig, int world, int rank, uint64_t epoch, int* err) {
+    pdl_wait();
+    pdl_trigger();
     if (threadIdx.x != 0) return;
     // this rank's peer parameter stores finished with the previous kernel
     asm volatile("fence.acq_rel.sys;" ::: "memory");
@@ -590,9 +596,9 @@ static cudaError_t set_smem_attr() {
 template <bool kMixed, bool kAg, bool kEma, bool kSgd>
 static void launch_apply_t(const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
                            const ApplyArgs& args, int grid, cudaStream_t stream, const AgArgs& ag) {
-    k_apply<kMixed, kAg, kEma, kSgd>
-        <<<grid, kApplyThreads, apply_smem_bytes(kMixed, kEma, kSgd), stream>>>(
-            chunks, n_chunks, n_vec, ctl, args, ag);
+    launch_pdl(k_apply<kMixed, kAg, kEma, kSgd>, dim3(grid), dim3(kApplyThreads),
+               apply_smem_bytes(kMixed, kEma, kSgd), stream, chunks, n_chunks, n_vec, ctl, args,
+               ag);
 }
 
 // The 16 instantiations, indexed by (mixed, ag, ema, sgd) bits.
@@ -628,13 +634,12 @@ cudaError_t prepare_kernels() {
 cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl* ctl,
                               double* partials, int grid, int use_scaler, double* out,
                               cudaStream_t stream) {
-    if (bf16)
-        k_grad_sumsq<true><<<grid, kThreads, 0, stream>>>(chunks, n_chunks, ctl, partials,
-                                                          use_scaler, out);
-    else
-        k_grad_sumsq<false><<<grid, kThreads, 0, stream>>>(chunks, n_chunks, ctl, partials,
-                                                           use_scaler, out);
-    return cudaGetLastError();
+    const cudaError_t e =
+        bf16 ? launch_pdl(k_grad_sumsq<true>, dim3(grid), dim3(kThreads), 0, stream, chunks,
+                          n_chunks, ctl, partials, use_scaler, out)
+             : launch_pdl(k_grad_sumsq<false>, dim3(grid), dim3(kThreads), 0, stream, chunks,
+                          n_chunks, ctl, partials, use_scaler, out);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
@@ -680,8 +685,9 @@ cudaError_t launch_step_done(Signals* const* sig, int world, int rank, uint64_t 
                              cudaStream_t stream) {
     SignalPtrs p{};
     for (int q = 0; q < world && q < kMaxRanks; ++q) p.q[q] = sig[q];
-    k_step_done<<<1, 32, 0, stream>>>(p, world, rank, epoch, err);
-    return cudaGetLastError();
+    const cudaError_t e = launch_pdl(k_step_done, dim3(1), dim3(32), 0, stream, p, world, rank,
+                                     epoch, err);
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t launch_wait_selftest(uint64_t limit_ns, int* out_error, unsigned long long* out_ns,

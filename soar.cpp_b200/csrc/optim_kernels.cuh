@@ -3,9 +3,31 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
+
 #include <cuda_runtime.h>
 
 namespace soarb {
+
+// Launches `kernel` with programmatic stream serialization: it may be
+// scheduled while the previous kernel on the stream drains (hiding the launch
+// gap between back-to-back kernels); the kernel itself waits for that
+// predecessor with griddepcontrol.wait before touching global memory.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Elements per chunk-table entry. A multiple of the tile, large enough that
 // the per-chunk descriptor read (64 B) is noise next to the 28 B/element the

@@ -132,6 +132,17 @@ __device__ __forceinline__ bool wait_flags(const uint64_t* flags, int n, uint64_
     }
 }
 
+// Programmatic dependent launch (griddepcontrol, sm_90+). Every kernel of the
+// step is launched with programmatic stream serialization (launch_pdl), so it
+// may be scheduled while the kernel before it on the stream drains; it calls
+// pdl_wait() before touching global memory, which returns once that kernel
+// has completed and its writes are visible (immediately when there is none).
+// pdl_trigger() lets the next kernel be scheduled as this one's CTAs retire.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Named barrier 1 over the kThreadsN consumer threads only.
 template <int kThreadsN>
 __device__ __forceinline__ void consumers_sync() {

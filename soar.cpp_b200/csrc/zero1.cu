@@ -155,6 +155,8 @@ k_rs_sumsq(const RsChunk* __restrict__ chunks, int n_chunks, int n_vec, RsArgs a
     constexpr int kConsumers = kRsConsumerWarps * 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int S = a.stages;
+    pdl_wait();
+    pdl_trigger();
     const float inv = a.use_scaler ? __fdiv_rn(1.0f, ctl->scale) : 1.0f;
     if (threadIdx.x == 0) {
         s_err = s_drain_err = 0;
@@ -545,9 +547,10 @@ SOAR_API int soar_zero1_reduce_sumsq(void* handle, double* d_partial, void* stre
     if (!handle || !d_partial) return fail("null argument");
     auto* z = static_cast<Zero1*>(handle);
     DeviceGuard g(z->device);
-    k_rs_sumsq<<<z->grid, kRsThreads, z->smem, static_cast<cudaStream_t>(stream)>>>(
-        z->d_chunks, z->n_chunks, z->n_vec, z->rs, z->ctl, z->partials, z->ticket, z->err,
-        d_partial);
+    Z1_CUDA_TRY(soarb::launch_pdl(k_rs_sumsq, dim3(z->grid), dim3(kRsThreads), z->smem,
+                                  static_cast<cudaStream_t>(stream), z->d_chunks, z->n_chunks,
+                                  z->n_vec, z->rs, z->ctl, z->partials, z->ticket, z->err,
+                                  d_partial));
     Z1_CUDA_TRY(cudaGetLastError());
     return SOAR_OK;
 }
@@ -589,8 +592,9 @@ SOAR_API int soar_zero1_step(void* handle, void* stream) {
     double* part = z->partials + z->grid;
     rs.parts_out = part + 1;
     rs.abort_out = reinterpret_cast<int*>(part + 1 + kMaxRanks);
-    k_rs_sumsq<<<z->grid, kRsThreads, z->smem, s>>>(z->d_chunks, z->n_chunks, z->n_vec, rs,
-                                                    z->ctl, z->partials, z->ticket, z->err, part);
+    Z1_CUDA_TRY(soarb::launch_pdl(k_rs_sumsq, dim3(z->grid), dim3(kRsThreads), z->smem, s,
+                                  z->d_chunks, z->n_chunks, z->n_vec, rs, z->ctl, z->partials,
+                                  z->ticket, z->err, part));
     Z1_CUDA_TRY(cudaGetLastError());
     const int rc = optim_apply_allgather(z->optim, rs.parts_out, z->world, s, z->ag, rs.abort_out);
     if (rc != SOAR_OK) return rc;
