@@ -239,6 +239,41 @@ void build_chunks(Optim& o) {
     o.host_chunks.insert(o.host_chunks.end(), scalar.begin(), scalar.end());
 }
 
+// The update hands chunks out dynamically from the top of the vector part of
+// the table down, so the chunks at its bottom are the last to be taken. Cut
+// those into short pieces (two tiles) until they hold kTailTilesPerCta tiles
+// per update CTA: the end of the step then balances at the granularity of a
+// piece rather than of a whole chunk, whatever the CTAs' relative speeds. The
+// pieces start at tile multiples of a vector chunk's start, so they stay
+// 16-byte aligned in every stream.
+constexpr uint64_t kTailTilesPerCta = 24;
+
+void split_tail(Optim& o, int grid) {
+    const size_t eb = elem_bytes(o);
+    const uint64_t piece = std::min<uint64_t>(2ull * soarb::kTile, o.chunk_elems);
+    const uint64_t want = kTailTilesPerCta * static_cast<uint64_t>(std::max(grid, 1));
+    std::vector<soarb::Chunk> out;
+    int k = 0;
+    uint64_t tiles = 0;
+    for (; k < o.n_vec && tiles < want; ++k) {
+        const soarb::Chunk& c = o.host_chunks[k];
+        for (uint64_t s = 0; s < c.n; s += piece) {
+            soarb::Chunk p = c;
+            p.n = static_cast<uint32_t>(std::min<uint64_t>(piece, c.n - s));
+            p.param = static_cast<char*>(c.param) + s * eb;
+            p.grad = static_cast<const char*>(c.grad) + s * eb;
+            // still the state offset (pointers are filled once the slab exists)
+            p.master = reinterpret_cast<float*>(reinterpret_cast<uintptr_t>(c.master) + s);
+            out.push_back(p);
+        }
+        tiles += (c.n + soarb::kTile - 1) / soarb::kTile;
+    }
+    const int pieces = static_cast<int>(out.size());
+    out.insert(out.end(), o.host_chunks.begin() + k, o.host_chunks.end());
+    o.n_vec += pieces - k;
+    o.host_chunks = std::move(out);
+}
+
 // Host-side check of the invariants the bulk-copy pipeline relies on, run on
 // the final chunk table before it is uploaded: every vector chunk is
 // non-empty, at most kChunkElems long, and all five of its streams start on a
@@ -327,6 +362,7 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
             choose_chunk_elems(total, sms * soarb::occupancy_apply(o->mixed, false, o->sgd));
     }
     build_chunks(*o);
+    split_tail(*o, sms * soarb::occupancy_apply(o->mixed, false, o->sgd));
     o->n_chunks = static_cast<int>(o->host_chunks.size());
     const int cap = std::max(1, o->n_chunks);
     o->grid_sumsq = std::min(sms * soarb::occupancy_grad_sumsq(o->mixed), cap);

@@ -250,20 +250,6 @@ __device__ __forceinline__ void apply_scalar(const Chunk& ch, uint32_t from, uin
     }
 }
 
-// Visits the pipelined tiles of this CTA in order: vector chunks from the end
-// of the vector part of the table, grid-strided, each in kTile pieces. The
-// producer and the consumers walk exactly this sequence.
-template <typename F>
-__device__ __forceinline__ void for_each_tile(const Chunk* chunks, int n_vec, F&& f) {
-    uint32_t q = 0;
-    for (int c = n_vec - 1 - static_cast<int>(blockIdx.x); c >= 0; c -= gridDim.x) {
-        const Chunk ch = chunks[c];
-        for (uint32_t t0 = 0; t0 < ch.n; t0 += kTile, ++q) {
-            if (!f(ch, t0, min(static_cast<uint32_t>(kTile), ch.n - t0), q)) return;
-        }
-    }
-}
-
 template <bool kMixed, bool kAg, bool kEma, bool kSgd>
 __global__ void __launch_bounds__(kApplyThreads, 1)
 k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restrict__ ctl,
@@ -279,6 +265,9 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
     __shared__ uint64_t s_t;
     __shared__ float s_norm;
     __shared__ uint32_t s_issued;
+    // per stage: the tile's chunk descriptor and (chunk index, tile offset)
+    __shared__ Chunk s_chunk[kStages];
+    __shared__ int2 s_tile[kStages];
 
     constexpr uint32_t kGradBytes = kMixed ? 2u : 4u;
     constexpr uint32_t kVecElems = kVecBytes / kGradBytes;  // elements per 16 B of grad
@@ -342,37 +331,69 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
     if (!s_skip) {
         if (warp == kConsumerWarps) {
             // ---- producer: one thread keeps the ring full -------------------
+            // Chunks are handed out dynamically, from the top of the vector
+            // part of the table down (the order k_grad_sumsq read last, so
+            // those gradients are still in L2): each grab is one atomic on
+            // Ctl::grab, taken one chunk ahead so its latency hides behind
+            // the current chunk's tiles. The table ends in short chunks
+            // (host-side), so CTAs that run slower or start later simply
+            // take fewer of them and all finish together. The chunk and the
+            // tile offset of every stage go to the consumers in shared memory
+            // (published by the same mbarrier arrive as the stage's bytes);
+            // a stage with chunk -1 tells them to stop.
             if (lane == 0) {
-                for_each_tile(chunks, n_vec, [&](const Chunk& ch, uint32_t t0, uint32_t len,
-                                                 uint32_t q) {
+                uint32_t q = 0;
+                auto produce = [&](int c, const Chunk& ch, uint32_t t0) -> bool {
                     const uint32_t s = q % kStages;
                     if (q >= kStages &&
                         !mbar_wait(smem_u32(&empty_bar[s]), ((q / kStages) + 1) & 1, &s_err))
                         return false;
-                    const uint32_t lv = len & ~(kVecElems - 1);
+                    s_chunk[s] = ch;
+                    s_tile[s] = make_int2(c, static_cast<int>(t0));
                     const uint32_t fb = smem_u32(&full_bar[s]);
-                    mbar_expect_tx(fb, stream_bytes * lv);
-                    if (lv) {
-                        const uint32_t base = smem_u32(smem + s * kStage);
-                        bulk_load(base, static_cast<const char*>(ch.grad) + kGradBytes * t0,
-                                  kGradBytes * lv, fb);
-                        bulk_load(base + kOffMaster, ch.master + t0, 4u * lv, fb);
-                        if (use_m) bulk_load(base + kOffM, ch.m + t0, 4u * lv, fb);
-                        if constexpr (!kSgd) bulk_load(base + kOffV, ch.v + t0, 4u * lv, fb);
-                        if constexpr (kEma) bulk_load(base + kOffE, ch.m + a.ema_delta + t0, 4u * lv, fb);
+                    if (c < 0) {
+                        mbar_arrive(fb);
+                    } else {
+                        const uint32_t len = min(static_cast<uint32_t>(kTile), ch.n - t0);
+                        const uint32_t lv = len & ~(kVecElems - 1);
+                        mbar_expect_tx(fb, stream_bytes * lv);
+                        if (lv) {
+                            const uint32_t base = smem_u32(smem + s * kStage);
+                            bulk_load(base, static_cast<const char*>(ch.grad) + kGradBytes * t0,
+                                      kGradBytes * lv, fb);
+                            bulk_load(base + kOffMaster, ch.master + t0, 4u * lv, fb);
+                            if (use_m) bulk_load(base + kOffM, ch.m + t0, 4u * lv, fb);
+                            if constexpr (!kSgd) bulk_load(base + kOffV, ch.v + t0, 4u * lv, fb);
+                            if constexpr (kEma)
+                                bulk_load(base + kOffE, ch.m + a.ema_delta + t0, 4u * lv, fb);
+                        }
                     }
-                    s_issued = q + 1;
+                    s_issued = ++q;
                     return true;
-                });
+                };
+                bool ok = true;
+                int c = n_vec - 1 - static_cast<int>(atomicAdd(&ctl->grab, 1u));
+                while (ok && c >= 0) {
+                    const Chunk ch = chunks[c];
+                    const int c_next = n_vec - 1 - static_cast<int>(atomicAdd(&ctl->grab, 1u));
+                    for (uint32_t t0 = 0; ok && t0 < ch.n; t0 += kTile) ok = produce(c, ch, t0);
+                    c = c_next;
+                }
+                if (ok) produce(-1, Chunk{}, 0u);
             }
         } else {
             // ---- consumers ---------------------------------------------------
             const uint32_t tid = threadIdx.x;
-            for_each_tile(chunks, n_vec, [&](const Chunk& ch, uint32_t t0, uint32_t len,
-                                             uint32_t q) {
+            for (uint32_t q = 0;; ++q) {
                 const uint32_t s = q % kStages;
-                const bool ok = mbar_wait(smem_u32(&full_bar[s]), (q / kStages) & 1, &s_err);
+                bool ok = mbar_wait(smem_u32(&full_bar[s]), (q / kStages) & 1, &s_err);
                 if (!ok) s_cfail[q & 1] = 1;
+                const int2 w = s_tile[s];
+                const bool stop = !ok || w.x < 0;  // the same for every consumer that waited
+                const Chunk ch = s_chunk[s];
+                const uint32_t t0 = static_cast<uint32_t>(w.y);
+                const uint32_t len = stop ? 0u : min(static_cast<uint32_t>(kTile), ch.n - t0);
+                ok = ok && !stop;
                 const uint32_t lv = len & ~(kVecElems - 1);
                 unsigned char* st = smem + s * kStage;
                 if (ok) {
@@ -434,7 +455,7 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                 // after the barrier every consumer reads the same failure flag
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 consumers_sync<kConsumers>();
-                if (s_cfail[q & 1]) return false;
+                if (s_cfail[q & 1] || stop) break;
                 if (tid == 0) {
                     if (lv) {
                         const uint32_t base = smem_u32(st);
@@ -459,8 +480,7 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                     }
                     mbar_arrive(smem_u32(&empty_bar[s]));
                 }
-                return true;
-            });
+            }
             if (tid == 0) bulk_wait_all();
             // scalar chunks (misaligned heads, mixed-phase tensors)
             for (int c = s_err ? n_chunks : n_vec + static_cast<int>(blockIdx.x); c < n_chunks; c += gridDim.x) {
@@ -509,6 +529,7 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                     }
                 }
             }
+            ctl->grab = 0u;  // every CTA has stopped grabbing
             ctl->ticket_apply = 0u;
         }
     }

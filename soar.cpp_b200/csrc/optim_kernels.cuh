@@ -77,6 +77,7 @@ struct __align__(64) Ctl {
     uint32_t ticket_sumsq;  // grid-reduction ticket of the sum-of-squares kernel
     uint32_t ticket_apply;  // completion ticket of the update kernel
     int32_t error;          // nonzero: a pipeline wait timed out (the step is incomplete)
+    uint32_t grab;          // chunks handed out so far by the running update (0 between launches)
 };
 
 // Per-launch arguments of the update kernel.
