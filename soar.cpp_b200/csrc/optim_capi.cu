@@ -169,7 +169,7 @@ int upload_bias_table(Optim& o, uint32_t len) {
 // chunks go first in the table (they feed the bulk-copy pipeline), scalar
 // chunks after them.
 // Chunk length: about 8 chunks per update CTA so small tensor lists still
-// spread over every SM and the grid-stride tail stays short, a power of two
+// spread over every SM and k_grad_sumsq's grid-stride tail stays short, a power of two
 // between one tile and kChunkElems (large lists keep kChunkElems).
 uint32_t choose_chunk_elems(uint64_t total_elems, int grid) {
     const uint64_t target = total_elems / (8ull * static_cast<uint64_t>(std::max(grid, 1)));

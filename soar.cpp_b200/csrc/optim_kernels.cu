@@ -20,10 +20,10 @@
 //                 AdamW moments, write master/m/v and the bf16 params back into
 //                 the stage, and one of them bulk-stores the stage to HBM. The
 //                 loads never wait on registers, so many tiles are in flight
-//                 per SM. Chunks are walked in the reverse order of
-//                 k_grad_sumsq so the gradients read last there are still in
-//                 L2. The last CTA to finish commits the step counters and the
-//                 loss-scaler update.
+//                 per SM. Chunks are handed out dynamically in the reverse
+//                 order of k_grad_sumsq, so the gradients read last there are
+//                 still in L2. The last CTA to finish commits the step
+//                 counters and the loss-scaler update.
 //
 // Numerics follow the reference's AdamW::step / clip_grad_norm
 // (src/optim/adamw.cpp:87-176) operation for operation with explicitly
