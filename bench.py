@@ -43,7 +43,7 @@ UNIT = "Gparams/s"
 # dram__bytes_read.sum + dram__bytes_write.sum of one k_apply launch on the full
 # 200M workload at N=1 (profiles/k_apply_config4.md: 2,801,499,392 read +
 # 2,740,448,512 written). Reported only for the workload it was measured on.
-APPLY_TRAFFIC_BYTES = {200_000_000: 5_541_947_904}
+APPLY_TRAFFIC_BYTES = {200_000_000: 5_541_141_760}
 
 
 def measured_peak_hbm() -> tuple[float, str]:

@@ -250,8 +250,22 @@ __device__ __forceinline__ void apply_scalar(const Chunk& ch, uint32_t from, uin
     }
 }
 
-template <bool kMixed, bool kAg, bool kEma, bool kSgd>
-__global__ void __launch_bounds__(kApplyThreads, 1)
+// Visits the pipelined tiles of this CTA in order: vector chunks from the end
+// of the vector part of the table, grid-strided, each in kTile pieces. The
+// producer and the consumers walk exactly this sequence (static hand-out).
+template <typename F>
+__device__ __forceinline__ void for_each_tile(const Chunk* chunks, int n_vec, F&& f) {
+    uint32_t q = 0;
+    for (int c = n_vec - 1 - static_cast<int>(blockIdx.x); c >= 0; c -= gridDim.x) {
+        const Chunk ch = chunks[c];
+        for (uint32_t t0 = 0; t0 < ch.n; t0 += kTile, ++q) {
+            if (!f(ch, t0, min(static_cast<uint32_t>(kTile), ch.n - t0), q)) return;
+        }
+    }
+}
+
+template <bool kMixed, bool kAg, bool kEma, bool kSgd, bool kDyn>
+__global__ void __launch_bounds__(kApplyThreads, 2)
 k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restrict__ ctl,
         ApplyArgs a, AgArgs ag) {
     extern __shared__ __align__(128) unsigned char smem[];
@@ -331,25 +345,19 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
     if (!s_skip) {
         if (warp == kConsumerWarps) {
             // ---- producer: one thread keeps the ring full -------------------
-            // Chunks are handed out dynamically, from the top of the vector
-            // part of the table down (the order k_grad_sumsq read last, so
-            // those gradients are still in L2): each grab is one atomic on
-            // Ctl::grab, taken one chunk ahead so its latency hides behind
-            // the current chunk's tiles. The table ends in short chunks
-            // (host-side), so CTAs that run slower or start later simply
-            // take fewer of them and all finish together. The chunk and the
-            // tile offset of every stage go to the consumers in shared memory
-            // (published by the same mbarrier arrive as the stage's bytes);
-            // a stage with chunk -1 tells them to stop.
             if (lane == 0) {
                 uint32_t q = 0;
+                // Issues tile t0 of chunk c (c < 0: the stop marker, kDyn only)
+                // into the next stage, once the consumers have released it.
                 auto produce = [&](int c, const Chunk& ch, uint32_t t0) -> bool {
                     const uint32_t s = q % kStages;
                     if (q >= kStages &&
                         !mbar_wait(smem_u32(&empty_bar[s]), ((q / kStages) + 1) & 1, &s_err))
                         return false;
-                    s_chunk[s] = ch;
-                    s_tile[s] = make_int2(c, static_cast<int>(t0));
+                    if constexpr (kDyn) {
+                        s_chunk[s] = ch;
+                        s_tile[s] = make_int2(c, static_cast<int>(t0));
+                    }
                     const uint32_t fb = smem_u32(&full_bar[s]);
                     if (c < 0) {
                         mbar_arrive(fb);
@@ -371,29 +379,49 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                     s_issued = ++q;
                     return true;
                 };
-                bool ok = true;
-                int c = n_vec - 1 - static_cast<int>(atomicAdd(&ctl->grab, 1u));
-                while (ok && c >= 0) {
-                    const Chunk ch = chunks[c];
-                    const int c_next = n_vec - 1 - static_cast<int>(atomicAdd(&ctl->grab, 1u));
-                    for (uint32_t t0 = 0; ok && t0 < ch.n; t0 += kTile) ok = produce(c, ch, t0);
-                    c = c_next;
+                if constexpr (kDyn) {
+                    // Chunks are handed out one atomic on Ctl::grab at a time,
+                    // from the top of the table down (the reverse of
+                    // k_grad_sumsq's order, so the gradients it read last are
+                    // still in L2). The next index and its descriptor are
+                    // fetched one chunk ahead. The table ends in short pieces,
+                    // so CTAs that run slower simply take fewer of them. Each
+                    // stage's chunk and tile offset reach the consumers in
+                    // shared memory, published by the stage's own mbarrier
+                    // arrive; chunk -1 tells them to stop.
+                    bool ok = true;
+                    int c = n_vec - 1 - static_cast<int>(atomicAdd(&ctl->grab, 1u));
+                    Chunk ch = c >= 0 ? chunks[c] : Chunk{};
+                    int c_next =
+                        c >= 0 ? n_vec - 1 - static_cast<int>(atomicAdd(&ctl->grab, 1u)) : -1;
+                    while (ok && c >= 0) {
+                        const Chunk ch_next = c_next >= 0 ? chunks[c_next] : Chunk{};
+                        const int c_after =
+                            c_next >= 0 ? n_vec - 1 - static_cast<int>(atomicAdd(&ctl->grab, 1u))
+                                        : -1;
+                        for (uint32_t t0 = 0; ok && t0 < ch.n; t0 += kTile)
+                            ok = produce(c, ch, t0);
+                        c = c_next;
+                        ch = ch_next;
+                        c_next = c_after;
+                    }
+                    if (ok) produce(-1, Chunk{}, 0u);
+                } else {
+                    // static walk: grid-strided from the top of the table; the
+                    // consumers walk the same sequence themselves
+                    for_each_tile(chunks, n_vec, [&](const Chunk& ch, uint32_t t0, uint32_t,
+                                                     uint32_t) { return produce(0, ch, t0); });
                 }
-                if (ok) produce(-1, Chunk{}, 0u);
             }
         } else {
             // ---- consumers ---------------------------------------------------
             const uint32_t tid = threadIdx.x;
-            for (uint32_t q = 0;; ++q) {
+            // Tile q (stage data already waited for). ok: compute it; stop:
+            // the sequence ends here (stop marker or a failed wait). Returns
+            // false when the consumers must leave the loop.
+            auto tile = [&](const Chunk& ch, uint32_t t0, uint32_t len, uint32_t q, bool ok,
+                            bool stop) -> bool {
                 const uint32_t s = q % kStages;
-                bool ok = mbar_wait(smem_u32(&full_bar[s]), (q / kStages) & 1, &s_err);
-                if (!ok) s_cfail[q & 1] = 1;
-                const int2 w = s_tile[s];
-                const bool stop = !ok || w.x < 0;  // the same for every consumer that waited
-                const Chunk ch = s_chunk[s];
-                const uint32_t t0 = static_cast<uint32_t>(w.y);
-                const uint32_t len = stop ? 0u : min(static_cast<uint32_t>(kTile), ch.n - t0);
-                ok = ok && !stop;
                 const uint32_t lv = len & ~(kVecElems - 1);
                 unsigned char* st = smem + s * kStage;
                 if (ok) {
@@ -455,7 +483,7 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                 // after the barrier every consumer reads the same failure flag
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 consumers_sync<kConsumers>();
-                if (s_cfail[q & 1] || stop) break;
+                if (s_cfail[q & 1] || stop) return false;
                 if (tid == 0) {
                     if (lv) {
                         const uint32_t base = smem_u32(st);
@@ -480,6 +508,28 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                     }
                     mbar_arrive(smem_u32(&empty_bar[s]));
                 }
+                return true;
+            };
+            if constexpr (kDyn) {
+                for (uint32_t q = 0;; ++q) {
+                    const uint32_t s = q % kStages;
+                    const bool ok = mbar_wait(smem_u32(&full_bar[s]), (q / kStages) & 1, &s_err);
+                    if (!ok) s_cfail[q & 1] = 1;
+                    const int2 w = s_tile[s];
+                    const bool stop = !ok || w.x < 0;  // the same for every consumer that waited
+                    const Chunk ch = s_chunk[s];
+                    const uint32_t t0 = static_cast<uint32_t>(w.y);
+                    const uint32_t len = stop ? 0u : min(static_cast<uint32_t>(kTile), ch.n - t0);
+                    if (!tile(ch, t0, len, q, !stop, stop)) break;
+                }
+            } else {
+                for_each_tile(chunks, n_vec, [&](const Chunk& ch, uint32_t t0, uint32_t len,
+                                                 uint32_t q) {
+                    const bool ok = mbar_wait(smem_u32(&full_bar[q % kStages]),
+                                              (q / kStages) & 1, &s_err);
+                    if (!ok) s_cfail[q & 1] = 1;
+                    return tile(ch, t0, len, q, ok, !ok);
+                });
             }
             if (tid == 0) bulk_wait_all();
             // scalar chunks (misaligned heads, mixed-phase tensors)
@@ -607,41 +657,45 @@ __global__ void k_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float sca
 
 // --------------------------------------------------------------- launchers --
 
-template <bool kMixed, bool kAg, bool kEma, bool kSgd>
+template <bool kMixed, bool kAg, bool kEma, bool kSgd, bool kDyn>
 static cudaError_t set_smem_attr() {
-    return cudaFuncSetAttribute(k_apply<kMixed, kAg, kEma, kSgd>,
+    return cudaFuncSetAttribute(k_apply<kMixed, kAg, kEma, kSgd, kDyn>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 static_cast<int>(apply_smem_bytes(kMixed, kEma, kSgd)));
 }
 
-template <bool kMixed, bool kAg, bool kEma, bool kSgd>
+template <bool kMixed, bool kAg, bool kEma, bool kSgd, bool kDyn>
 static void launch_apply_t(const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
                            const ApplyArgs& args, int grid, cudaStream_t stream, const AgArgs& ag) {
-    launch_pdl(k_apply<kMixed, kAg, kEma, kSgd>, dim3(grid), dim3(kApplyThreads),
+    launch_pdl(k_apply<kMixed, kAg, kEma, kSgd, kDyn>, dim3(grid), dim3(kApplyThreads),
                apply_smem_bytes(kMixed, kEma, kSgd), stream, chunks, n_chunks, n_vec, ctl, args,
                ag);
 }
 
-// The 16 instantiations, indexed by (mixed, ag, ema, sgd) bits.
+// The 32 instantiations, indexed by (mixed, ag, ema, sgd, dyn) bits.
 using SetFn = cudaError_t (*)();
 using LaunchFn = void (*)(const Chunk*, int, int, Ctl*, const ApplyArgs&, int, cudaStream_t,
                           const AgArgs&);
-#define SOARB_VARIANT(b)                                                                      \
-    {set_smem_attr<(b & 8) != 0, (b & 4) != 0, (b & 2) != 0, (b & 1) != 0>,                   \
-     launch_apply_t<(b & 8) != 0, (b & 4) != 0, (b & 2) != 0, (b & 1) != 0>}
+#define SOARB_VARIANT(b)                                                                    \
+    {set_smem_attr<(b & 16) != 0, (b & 8) != 0, (b & 4) != 0, (b & 2) != 0, (b & 1) != 0>, \
+     launch_apply_t<(b & 16) != 0, (b & 8) != 0, (b & 4) != 0, (b & 2) != 0, (b & 1) != 0>}
 struct Variant {
     SetFn set;
     LaunchFn launch;
 };
-static const Variant kVariants[16] = {
+static const Variant kVariants[32] = {
     SOARB_VARIANT(0),  SOARB_VARIANT(1),  SOARB_VARIANT(2),  SOARB_VARIANT(3),
     SOARB_VARIANT(4),  SOARB_VARIANT(5),  SOARB_VARIANT(6),  SOARB_VARIANT(7),
     SOARB_VARIANT(8),  SOARB_VARIANT(9),  SOARB_VARIANT(10), SOARB_VARIANT(11),
-    SOARB_VARIANT(12), SOARB_VARIANT(13), SOARB_VARIANT(14), SOARB_VARIANT(15)};
+    SOARB_VARIANT(12), SOARB_VARIANT(13), SOARB_VARIANT(14), SOARB_VARIANT(15),
+    SOARB_VARIANT(16), SOARB_VARIANT(17), SOARB_VARIANT(18), SOARB_VARIANT(19),
+    SOARB_VARIANT(20), SOARB_VARIANT(21), SOARB_VARIANT(22), SOARB_VARIANT(23),
+    SOARB_VARIANT(24), SOARB_VARIANT(25), SOARB_VARIANT(26), SOARB_VARIANT(27),
+    SOARB_VARIANT(28), SOARB_VARIANT(29), SOARB_VARIANT(30), SOARB_VARIANT(31)};
 #undef SOARB_VARIANT
 
-static int variant_index(bool mixed, bool ag, bool ema, bool sgd) {
-    return (mixed ? 8 : 0) | (ag ? 4 : 0) | (ema ? 2 : 0) | (sgd ? 1 : 0);
+static int variant_index(bool mixed, bool ag, bool ema, bool sgd, bool dyn) {
+    return (mixed ? 16 : 0) | (ag ? 8 : 0) | (ema ? 4 : 0) | (sgd ? 2 : 0) | (dyn ? 1 : 0);
 }
 
 cudaError_t prepare_kernels() {
@@ -665,9 +719,9 @@ cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl*
 
 cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
                          const ApplyArgs& args, int grid, cudaStream_t stream, const AgArgs* ag,
-                         bool ema, bool sgd) {
+                         bool ema, bool sgd, bool dyn) {
     const AgArgs none{};
-    kVariants[variant_index(mixed, ag != nullptr, ema, sgd)].launch(
+    kVariants[variant_index(mixed, ag != nullptr, ema, sgd, dyn)].launch(
         chunks, n_chunks, n_vec, ctl, args, grid, stream, ag ? *ag : none);
     return cudaGetLastError();
 }
@@ -729,7 +783,7 @@ int occupancy_grad_sumsq(bool bf16) {
 template <bool kMixed, bool kEma, bool kSgd>
 static int occupancy_t() {
     int n = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<kMixed, false, kEma, kSgd>,
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply<kMixed, false, kEma, kSgd, false>,
                                                   kApplyThreads,
                                                   apply_smem_bytes(kMixed, kEma, kSgd));
     return n;

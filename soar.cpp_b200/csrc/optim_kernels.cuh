@@ -156,10 +156,12 @@ cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl*
                               cudaStream_t stream);
 // ag == nullptr: plain update; otherwise the update with the fused all-gather.
 // ema: also update the weight EMA shadow (args.ema_*). sgd: the SGD update
-// (args.momentum/omdamp/nesterov) instead of AdamW.
+// (args.momentum/omdamp/nesterov) instead of AdamW. dyn: hand the chunks out
+// dynamically (Ctl::grab) instead of the static grid-strided walk.
 cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
                          const ApplyArgs& args, int grid, cudaStream_t stream,
-                         const AgArgs* ag = nullptr, bool ema = false, bool sgd = false);
+                         const AgArgs* ag = nullptr, bool ema = false, bool sgd = false,
+                         bool dyn = false);
 cudaError_t launch_scale_grads_f32(const Chunk* chunks, int n_chunks, float coef, int grid,
                                    cudaStream_t stream);
 cudaError_t launch_bf16_to_f32(const uint16_t* src, float* dst, uint64_t n,
