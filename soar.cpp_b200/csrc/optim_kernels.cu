@@ -20,10 +20,12 @@
 //                 AdamW moments, write master/m/v and the bf16 params back into
 //                 the stage, and one of them bulk-stores the stage to HBM. The
 //                 loads never wait on registers, so many tiles are in flight
-//                 per SM. Chunks are handed out dynamically in the reverse
-//                 order of k_grad_sumsq, so the gradients read last there are
-//                 still in L2. The last CTA to finish commits the step
-//                 counters and the loss-scaler update.
+//                 per SM. Chunks are taken from the top of the table down --
+//                 the reverse of k_grad_sumsq's order, so the gradients read
+//                 last there are still in L2 -- either by a static
+//                 grid-strided walk or handed out dynamically (one atomic per
+//                 chunk; chosen per optimizer on the host). The last CTA to
+//                 finish commits the step counters and the loss-scaler update.
 //
 // Numerics follow the reference's AdamW::step / clip_grad_norm
 // (src/optim/adamw.cpp:87-176) operation for operation with explicitly
@@ -279,9 +281,9 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
     __shared__ uint64_t s_t;
     __shared__ float s_norm;
     __shared__ uint32_t s_issued;
-    // per stage: the tile's chunk descriptor and (chunk index, tile offset)
-    __shared__ Chunk s_chunk[kStages];
-    __shared__ int2 s_tile[kStages];
+    // (dynamic hand-out) per stage: the tile's chunk descriptor and (chunk index, tile offset)
+    __shared__ Chunk s_chunk[kDyn ? kStages : 1];
+    __shared__ int2 s_tile[kDyn ? kStages : 1];
 
     constexpr uint32_t kGradBytes = kMixed ? 2u : 4u;
     constexpr uint32_t kVecElems = kVecBytes / kGradBytes;  // elements per 16 B of grad
