@@ -189,6 +189,13 @@ SOAR_API int soar_optim_get_lr(void* handle, float* out_lr);
    beyond get_lr; the reference keeps step_count_ private (adamw.hpp:35). */
 SOAR_API int soar_optim_get_info(void* handle, soar_step_info* out, void* stream);
 
+/* The same bookkeeping without synchronising the host: enqueues on `stream`
+   a copy of the values as they stand once the stream's earlier work (the
+   step) has run; they are in *out when an event recorded on `stream` after
+   this call has completed. `out` should be pinned host memory
+   (cudaHostAlloc) for the copy to stay asynchronous. */
+SOAR_API int soar_optim_get_info_async(void* handle, soar_step_info* out, void* stream);
+
 /* Restores step count, skip count, loss scale and growth tracker (resume). */
 SOAR_API int soar_optim_set_counters(void* handle, uint64_t step, uint64_t skipped,
                                      float loss_scale, int32_t growth_tracker, void* stream);

@@ -87,6 +87,7 @@ struct Optim {
     double* partials = nullptr;
     soarb::Ctl* ctl = nullptr;
     double* sumsq_scratch = nullptr;
+    soar_step_info* info_stage = nullptr;  // device staging of soar_optim_get_info_async
 
     float* ema = nullptr;        // weight-EMA shadow (separate allocation, state layout)
     float ema_decay = 0.0f;
@@ -416,6 +417,8 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
     off = align_up(off + sizeof(soarb::Ctl), kSlabAlign);
     const size_t off_scratch = off;
     off = align_up(off + sizeof(double), kSlabAlign);
+    const size_t off_info = off;
+    off = align_up(off + sizeof(soar_step_info), kSlabAlign);
 
     cudaError_t e = cudaMalloc(&o->slab, off);
     if (e != cudaSuccess) {
@@ -431,6 +434,7 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
     o->partials = reinterpret_cast<double*>(o->slab + off_partials);
     o->ctl = reinterpret_cast<soarb::Ctl*>(o->slab + off_ctl);
     o->sumsq_scratch = reinterpret_cast<double*>(o->slab + off_scratch);
+    o->info_stage = reinterpret_cast<soar_step_info*>(o->slab + off_info);
 
     for (auto* table : {&o->host_chunks, &o->host_sumsq_chunks}) {
         for (soarb::Chunk& c : *table) {
@@ -551,6 +555,21 @@ int sumsq_impl(Optim& o, double* out, cudaStream_t s) {
 
 Optim* as_optim(void* h) { return static_cast<Optim*>(h); }
 
+}  // namespace
+
+namespace {
+// Packs the control block into the public soar_step_info layout, on the stream.
+__global__ void k_pack_info(const soarb::Ctl* c, soar_step_info* out) {
+    out->step = c->t;
+    out->skipped = c->skipped;
+    out->grad_norm = c->last_norm;
+    out->found_inf = c->last_found_inf;
+    out->clip_coef = c->last_clip_coef;
+    out->loss_scale = c->scale;
+    out->growth_tracker = c->tracker;
+    out->lr = c->last_lr;
+    out->error = c->error;
+}
 }  // namespace
 
 namespace soarb {
@@ -789,6 +808,17 @@ SOAR_API int soar_optim_get_info(void* handle, soar_step_info* out, void* stream
     out->growth_tracker = c.tracker;
     out->lr = c.last_lr;
     out->error = c.error;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_optim_get_info_async(void* handle, soar_step_info* out, void* stream) {
+    if (!handle || !out) return fail("null argument");
+    Optim& o = *as_optim(handle);
+    DeviceGuard g(o.device);
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    k_pack_info<<<1, 1, 0, s>>>(o.ctl, o.info_stage);
+    SOAR_CUDA_TRY(cudaGetLastError());
+    SOAR_CUDA_TRY(cudaMemcpyAsync(out, o.info_stage, sizeof *out, cudaMemcpyDeviceToHost, s));
     return SOAR_OK;
 }
 

@@ -84,6 +84,7 @@ SIGNATURES: dict[str, tuple] = {
     "soar_optim_set_lr": (C.c_int, [C.c_void_p, C.c_float]),
     "soar_optim_get_lr": (C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),
     "soar_optim_get_info": (C.c_int, [C.c_void_p, C.POINTER(StepInfo), C.c_void_p]),
+    "soar_optim_get_info_async": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     "soar_optim_set_counters": (C.c_int, [C.c_void_p, C.c_uint64, C.c_uint64, C.c_float,
                                           C.c_int32, C.c_void_p]),
     "soar_optim_state_ptr": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_void_p)]),
@@ -326,6 +327,24 @@ class AdamW:
         _check(lib().soar_optim_get_info(self.handle, C.byref(out), _stream_handle(stream)),
                "soar_optim_get_info")
         return out
+
+    def info_async(self, stream=None):
+        """Enqueue the bookkeeping readback without synchronising the host.
+        Returns (info, event): `info` is a StepInfo in pinned host memory,
+        valid once `event` (recorded on the stream after the readback) has
+        completed."""
+        import torch
+        buf = torch.empty(C.sizeof(StepInfo), dtype=torch.uint8).pin_memory()
+        _check(lib().soar_optim_get_info_async(self.handle, buf.data_ptr(), _stream_handle(stream)),
+               "soar_optim_get_info_async")
+        ev = torch.cuda.Event()
+        s = torch.cuda.current_stream(self.device) if stream is None else stream
+        if isinstance(s, int):
+            s = torch.cuda.ExternalStream(s)
+        ev.record(s)
+        info = StepInfo.from_address(buf.data_ptr())
+        info._keepalive = buf
+        return info, ev
 
     def set_counters(self, step: int, skipped: int, loss_scale: float, growth_tracker: int,
                      stream=None) -> None:

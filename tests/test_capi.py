@@ -61,6 +61,7 @@ def test_null_arguments_return_error():
     assert lib.soar_optim_step(None, None) == -1
     assert b"null" in lib.soar_last_error()
     assert lib.soar_optim_set_lr(None, 1.0) == -1
+    assert lib.soar_optim_get_info_async(None, None, None) == -1
     assert lib.soar_cosine_step(None) == -1
     out = ctypes.c_void_p()
     assert lib.soar_optim_create(None, 1, None, ctypes.byref(out)) == -1

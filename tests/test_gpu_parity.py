@@ -224,3 +224,25 @@ def test_errors_are_reported(cuda):
     with pytest.raises(sb.SoarError):
         sb.AdamW([p], layout="bf16_mixed", grads=[torch.zeros(4, device="cuda")],
                  loss_scaler=sb.LossScalerOptions(init_scale=-1.0))
+
+
+def test_async_info_matches_sync(cuda):
+    """soar_optim_get_info_async: the readback enqueued on the stream (pinned
+    host memory, read after an event) equals the synchronous readback, step by
+    step, through skips and scale changes."""
+    torch = cuda
+    case = cases.mixed_small(steps=8)
+    run = GpuRun(torch, case)
+    scale = case.init_scale
+    for t in range(1, case.steps + 1):
+        run.load_grads(case.grads(t, scale))
+        run.opt.step()
+        info, ev = run.opt.info_async()
+        ev.synchronize()
+        want = run.opt.info()
+        assert (info.step, info.skipped, info.loss_scale, info.found_inf, info.growth_tracker,
+                info.error) == (want.step, want.skipped, want.loss_scale, want.found_inf,
+                                want.growth_tracker, want.error)
+        assert info.grad_norm == want.grad_norm and info.clip_coef == want.clip_coef
+        scale = want.loss_scale
+    run.opt.close()
