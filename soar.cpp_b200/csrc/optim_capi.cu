@@ -257,9 +257,19 @@ void build_chunks(Optim& o) {
 bool choose_dynamic(const Optim& o, int grid) {
     if (!o.mixed) return true;
     int with_grad = 0;
+    uint64_t total = 0;
     for (const TensorRec& t : o.tensors)
-        if (t.grad && t.numel) ++with_grad;
-    return with_grad >= std::max(grid, 1) / 4;
+        if (t.grad && t.numel) {
+            ++with_grad;
+            total += t.numel;
+        }
+    // one to four tensors (the config-5 shape): dynamic measured ~3-4 % faster at
+    // 16M-64M params, static faster at <= 4M (fewer atomics per tile) and at
+    // >= 200M. (ZeRO-1 shards, a handful of bucket slices, keep the static walk
+    // measured on NVLink.)
+    constexpr uint64_t kDynLo = 8ull << 20, kDynHi = 96ull << 20;
+    return with_grad >= std::max(grid, 1) / 4 ||
+           (with_grad <= 4 && total >= kDynLo && total < kDynHi);
 }
 
 // The dynamic hand-out goes from the top of the vector part of the table
