@@ -67,6 +67,9 @@ def parse():
                     help="config 5: flat 1M..2B params in both layouts, one JSON line each "
                          "(not the headline line)")
     ap.add_argument("--sweep-sizes", default="1000000,16000000,256000000,1000000000,2000000000")
+    ap.add_argument("--cpu-sample", action="store_true",
+                    help="print the CPU reference sample of --params params as JSON and exit "
+                         "(threads from OMP_NUM_THREADS; the 1-thread baseline row runs this)")
     ap.add_argument("--configs", action="store_true",
                     help="configs 1-3 at their own shapes on one GPU, one JSON line each "
                          "(not the headline line)")
@@ -88,7 +91,7 @@ def cpu_reference_sample(n: int, steps: int, warmup: int = 1) -> dict:
 
     from oracle import oracle
     from soar_b200 import synth
-    threads = os.cpu_count() or 1
+    threads = int(os.environ.get("OMP_NUM_THREADS", "0")) or (os.cpu_count() or 1)
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
     p = synth.normal(synth.seed_of(4, 0), n, 0.02)
     g = synth.normal(synth.seed_of(4, 1, 0), n, 1e-3)
@@ -116,6 +119,20 @@ def cpu_reference_sample(n: int, steps: int, warmup: int = 1) -> dict:
             "sample": f"{steps} steps of clip_grad_norm(1.0)+step() on one fp32 bucket of "
                       f"{n} params (host arrays, unscale/bf16 cast not timed)",
             "ms_per_step": dt / steps * 1e3}
+
+
+def cpu_single_thread_sample(n: int, steps: int = 3) -> dict | None:
+    """The same sample on one host thread, in a child process (OpenMP reads
+    OMP_NUM_THREADS when the library starts)."""
+    env = dict(os.environ, OMP_NUM_THREADS="1")
+    r = subprocess.run([sys.executable, str(Path(__file__).resolve()), "--cpu-sample",
+                        "--params", str(n), "--steps", str(steps)],
+                       env=env, capture_output=True, text=True, timeout=300)
+    lines = [x for x in r.stdout.splitlines() if x.startswith("{")]
+    if r.returncode != 0 or not lines:
+        return None
+    d = json.loads(lines[-1])
+    return {"value": d["value"], "cores": d["cores"], "sample": d["sample"]}
 
 
 def run_reference(args):
@@ -442,6 +459,7 @@ def run_ours(args):
         try:
             cpu = cpu_reference_sample(min(BUCKET, n), 5)
             cpu.pop("ms_per_step", None)
+            cpu["single_thread"] = cpu_single_thread_sample(min(BUCKET, n) // 5)
         except Exception as ex:  # the baseline is reported, never required
             cpu = {"error": str(ex)}
 
@@ -766,6 +784,10 @@ def run_configs(args):
 
 def main():
     args = parse()
+    if args.cpu_sample:
+        res = cpu_reference_sample(args.params, args.steps)
+        print(json.dumps(res), flush=True)
+        return 0
     if args.impl == "reference":
         return run_reference(args)
     if args.sweep:
