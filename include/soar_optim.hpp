@@ -115,6 +115,11 @@ public:
         detail::check(soar_optim_get_info(h_, &i, stream), "get_info");
         return i;
     }
+    // Enqueues the same readback on `stream` into caller-owned (pinned) host
+    // memory; *out is valid once an event recorded after this call completes.
+    void info_async(soar_step_info* out, void* stream = nullptr) const {
+        detail::check(soar_optim_get_info_async(h_, out, stream), "get_info_async");
+    }
     [[nodiscard]] void* handle() const noexcept { return h_; }
 
 private:
