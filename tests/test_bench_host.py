@@ -1,0 +1,81 @@
+"""Host-side pieces of bench.py that need no GPU: the clock summary taken
+during the timed region (NVML samples and the nvidia-smi fallback) and the
+CPU reference sample used by the baseline rows."""
+import io
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+import bench  # noqa: E402
+
+
+def test_clock_summary_uses_only_samples_inside_the_timed_region():
+    cs = bench.ClockSampler([0, 1])
+    cs.thread = type("T", (), {"join": lambda self, t=None: None})()  # no real thread
+    cs.max_mhz = [1965, 1965]
+    # idle before, loaded inside [10, 11], a throttle reason only outside
+    cs.samples = [(9.0, 0, 600.0, []), (9.0, 1, 600.0, ["sw_power_cap"]),
+                  (10.1, 0, 1965.0, []), (10.1, 1, 1950.0, ["sw_power_cap"]),
+                  (10.6, 0, 1965.0, []), (10.6, 1, 1965.0, []),
+                  (12.0, 0, 700.0, ["hw_slowdown"])]
+    cs.window = [10.0, 11.0]
+    out = cs.stop()
+    assert out["samples"] == 4
+    assert out["sm_mhz"] == 1965.0
+    assert out["sm_max_mhz"] == 1965
+    assert out["reasons"] == ["sw_power_cap"]
+    assert out["source"] == "nvml"
+
+
+def test_clock_summary_falls_back_to_the_nearest_sample_after_a_short_region():
+    cs = bench.ClockSampler([0])
+    cs.thread = type("T", (), {"join": lambda self, t=None: None})()
+    cs.max_mhz = [1965]
+    cs.samples = [(1.0, 0, 500.0, []), (2.02, 0, 1965.0, []), (3.0, 0, 1800.0, [])]
+    cs.window = [2.0, 2.01]  # shorter than the sampling period, nothing inside
+    out = cs.stop()
+    assert out["samples"] == 1 and out["sm_mhz"] == 1965.0
+
+
+def test_clock_summary_parses_the_nvidia_smi_fallback(tmp_path):
+    cs = bench.ClockSampler([0, 1])
+    cs.fh = io.StringIO("0, 1965, 1965, Not Active, Not Active, Not Active, Active\n"
+                        "1, 1900, 1965, Active, Not Active, Not Active, Not Active\n"
+                        "2, 100, 1965, Active, Active, Active, Active\n"   # not our GPU
+                        "garbage line\n")
+
+    class P:
+        def terminate(self):
+            pass
+
+        def wait(self, t=None):
+            return 0
+    cs.proc = P()
+    out = cs.stop()
+    assert out["samples"] == 2
+    assert out["sm_max_mhz"] == 1965.0
+    assert out["reasons"] == ["hw_slowdown", "sw_power_cap"]
+    assert out["source"] == "nvidia-smi"
+
+
+def test_cpu_reference_sample_reports_the_reference_kind_and_threads():
+    res = bench.cpu_reference_sample(200_000, 2, warmup=1)
+    assert res["value"] > 0 and res["unit"] == bench.UNIT
+    assert res["kind"] in ("reference", "port") and res["cores"] >= 1
+
+
+def test_cpu_sample_child_runs_on_one_thread():
+    env = dict(os.environ, OMP_NUM_THREADS="1")
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--cpu-sample", "--params",
+                        "100000", "--steps", "2"], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    d = json.loads([x for x in r.stdout.splitlines() if x.startswith("{")][-1])
+    assert d["cores"] == 1 and d["value"] > 0
