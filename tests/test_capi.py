@@ -5,6 +5,8 @@ import re
 import subprocess
 from pathlib import Path
 
+import pytest
+
 import soar_b200 as sb
 from soar_b200 import _build, optim
 
@@ -88,3 +90,28 @@ def test_data_parallel_entry_points_reject_bad_arguments():
     big = (ctypes.c_void_p * 8)(*[16 * (i + 1) for i in range(8)])
     assert lib.soar_nvlink_probe(big, 8, 0, 1 << 20, 0, 16384, 2, 1, ctypes.byref(err), None) == -1
     assert b"ring" in lib.soar_last_error()
+
+
+def test_header_is_plain_c_and_links(tmp_path):
+    """include/soar_optim.h is a C header (C99, pedantic) and a C program links
+    against the library with it."""
+    import shutil
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if not cc:
+        pytest.skip("no C compiler")
+    src = tmp_path / "c_user.c"
+    src.write_text('#include "soar_optim.h"\n'
+                   "int main(void) {\n"
+                   "    soar_adamw_opts o;\n"
+                   "    soar_adamw_default_opts(&o);\n"
+                   "    return soar_optim_step(0, 0) == SOAR_ERROR && o.lr > 0.0f ? 0 : 1;\n"
+                   "}\n")
+    lib = _build.build()
+    inc = Path(__file__).resolve().parents[1] / "include"
+    exe = tmp_path / "c_user"
+    r = subprocess.run([cc, "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", str(inc),
+                        str(src), "-o", str(exe), "-L", str(lib.parent), "-lsoar_optim",
+                        f"-Wl,-rpath,{lib.parent}"], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stderr
