@@ -115,3 +115,36 @@ def test_header_is_plain_c_and_links(tmp_path):
     assert r.returncode == 0, r.stderr
     run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
     assert run.returncode == 0, run.stderr
+
+
+def test_ctypes_structs_match_the_c_layout(tmp_path):
+    """The Python binding's structs (soar_b200/optim.py) have the C header's
+    size and field offsets, as a C compiler lays them out."""
+    import shutil
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if not cc:
+        pytest.skip("no C compiler")
+    pairs = [("soar_tensor_desc", optim.TensorDesc), ("soar_adamw_opts", optim.AdamWOpts),
+             ("soar_sgd_opts", optim.SGDOpts), ("soar_step_info", optim.StepInfo),
+             ("soar_zero1_shard", optim.Zero1Shard)]
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "soar_optim.h"',
+             "int main(void) {"]
+    for cname, py in pairs:
+        lines.append(f'    printf("{cname} size %zu\\n", sizeof({cname}));')
+        for f, _ in py._fields_:
+            lines.append(f'    printf("{cname} {f} %zu\\n", offsetof({cname}, {f}));')
+    lines += ["    return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    r = subprocess.run([cc, "-std=c99", "-I", str(ROOT / "include"), str(src), "-o", str(exe)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    got = {}
+    for ln in subprocess.run([str(exe)], capture_output=True, text=True).stdout.splitlines():
+        name, field, val = ln.split()
+        got[(name, field)] = int(val)
+    for cname, py in pairs:
+        assert got[(cname, "size")] == ctypes.sizeof(py), cname
+        for f, _ in py._fields_:
+            assert got[(cname, f)] == getattr(py, f).offset, (cname, f)
