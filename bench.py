@@ -421,7 +421,12 @@ def run_ours(args):
     if comm:
         torch.distributed.all_reduce(ph, op=torch.distributed.ReduceOp.MAX)
     phases = {k: round(float(v), 4) for k, v in zip(phase_names, ph.tolist())}
-    nvl = nvlink_rates(torch, world, rank, local, 2 * shard_params, phases) if fused else None
+    nvl = None
+    if fused:
+        try:  # a reported roofline, never a reason to lose the bench line
+            nvl = nvlink_rates(torch, world, rank, local, 2 * shard_params, phases)
+        except Exception as ex:
+            nvl = {"error": str(ex)[:300]}
     if apply_ms is None:  # device-synchronised step: the update phase of the loop above
         apply_ms = [float(ph[phase_names.index("update+allgather")])]
     t = torch.tensor([ms, statistics.mean(apply_ms)], dtype=torch.float64, device=dev)
