@@ -15,9 +15,23 @@ second.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Rank 0 prints one JSON line. `--impl reference` times the reference's own CPU
-AdamW (oracle/_ref: the unmodified src/optim/adamw.cpp; the port oracle if that
-was not built) on a bounded sample of the same workload with all host threads.
+Rank 0 prints one JSON line. Besides the timed step it carries:
+  e2e       the same step through the public API with host buffers: every
+            step copies the rank's gradient in from pinned memory and its
+            updated params out, on two copy streams so that the read-back of
+            step s overlaps the upload of step s+1;
+  roofline  k_apply against the measured HBM copy peak at N = 1; the two
+            fused collective kernels against NVLink at N > 1 (HBM secondary);
+  parity    after the timed region, one more step checked against the CPU
+            oracle on a sample of rank 0's shard, plus bit-identical params and
+            counters on every rank;
+  configs   (N = 1) BASELINE configs 1-3 and config-5 sizes, each step timed
+            alone after an L2 flush.
+
+`--impl reference` times the reference's own CPU AdamW (oracle/_ref: the
+unmodified src/optim/adamw.cpp; the port oracle if that was not built) on the
+same 200M-parameter workload (8 fp32 buckets of 25M) with every host thread,
+in a child process that loads nothing of this package.
 """
 from __future__ import annotations
 
@@ -40,10 +54,16 @@ BUCKET = 25_000_000
 BYTES_PER_PARAM = 28          # algorithmic: read g 2 + master/m/v 12, write master/m/v 12 + param 2
 METRIC = "AdamW Gparams/s (fused ZeRO-1 optimizer step, 200M bf16-mixed params)"
 UNIT = "Gparams/s"
-# dram__bytes_read.sum + dram__bytes_write.sum of one k_apply launch on the full
-# 200M workload at N=1 (profiles/k_apply_config4.md: 2,801,499,392 read +
-# 2,740,448,512 written). Reported only for the workload it was measured on.
+# dram__bytes_read.sum + dram__bytes_write.sum of one k_apply launch on the
+# full 200M-parameter shard at N = 1, from a one-pass ncu capture of this
+# bench's own command (2,801,499,392 read + 2,740,448,512 written). Reported
+# only for the workload it was measured on.
 APPLY_TRAFFIC_BYTES = {200_000_000: 5_541_141_760}
+# NVLink references of this pool (per direction per GPU): the measured peer
+# copy and NVLink 5's specification.
+NVLINK_PEER_COPY_GBS = 770.0
+NVLINK_SPEC_GBS = 900.0
+L2_FLUSH_BYTES = 256 << 20    # twice the 126 MB L2
 
 
 def measured_peak_hbm() -> tuple[float, str]:
@@ -54,6 +74,14 @@ def measured_peak_hbm() -> tuple[float, str]:
         return 6650.0, "fallback"
 
 
+def host_threads() -> int:
+    """Every host CPU this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -61,17 +89,19 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--params", type=int, default=N_PARAMS)
-    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-steps", type=int, default=6)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="leave the configs key out of the N=1 line")
     ap.add_argument("--sweep", action="store_true",
                     help="config 5: flat 1M..2B params in both layouts, one JSON line each "
                          "(not the headline line)")
     ap.add_argument("--sweep-sizes", default="1000000,16000000,256000000,1000000000,2000000000")
     ap.add_argument("--cpu-sample", action="store_true",
-                    help="print the CPU reference sample of --params params as JSON and exit "
-                         "(threads from OMP_NUM_THREADS; the 1-thread baseline row runs this)")
+                    help="(child process) time the CPU reference on --params params and print "
+                         "JSON; threads from OMP_NUM_THREADS")
     ap.add_argument("--configs", action="store_true",
-                    help="configs 1-3 at their own shapes on one GPU, one JSON line each "
+                    help="configs 1-3 and config-5 sizes on one GPU, one JSON line each "
                          "(not the headline line)")
     ap.add_argument("--dp", default="fused", choices=["fused", "fused-nccl", "nccl"],
                     help="N>1: collectives fused into the kernels over peer memory, the ranks "
@@ -84,19 +114,20 @@ def parse():
 # ------------------------------------------------------------ CPU baseline --
 
 def cpu_reference_sample(n: int, steps: int, warmup: int = 1) -> dict:
-    """The reference's clip_grad_norm(1.0) + step() (adamw.cpp:87-176) on one
-    fp32 bucket of n params (the unscaled grads and fp32 master of the mixed
-    workload), OpenMP over all host threads. Returns Gparams/s."""
+    """The reference's clip_grad_norm(1.0) + step() (adamw.cpp:28-117) on n
+    fp32 params cut into 25M-element buckets (the unscaled grads and fp32
+    master of the mixed workload), OpenMP over OMP_NUM_THREADS threads. Inputs
+    come from numpy; nothing of this package is loaded. Returns Gparams/s."""
     import numpy as np
 
     from oracle import oracle
-    from soar_b200 import synth
-    threads = int(os.environ.get("OMP_NUM_THREADS", "0")) or (os.cpu_count() or 1)
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
-    p = synth.normal(synth.seed_of(4, 0), n, 0.02)
-    g = synth.normal(synth.seed_of(4, 1, 0), n, 1e-3)
+    threads = int(os.environ.get("OMP_NUM_THREADS", "0")) or host_threads()
+    rng = np.random.Generator(np.random.PCG64(4))
+    sizes = [min(BUCKET, n - s) for s in range(0, n, BUCKET)]
+    ps = [rng.standard_normal(k, dtype=np.float32) * np.float32(0.02) for k in sizes]
+    gs = [rng.standard_normal(k, dtype=np.float32) * np.float32(1e-3) for k in sizes]
     if oracle.ref_available():
-        opt = oracle.RefAdamW([p], [g], lr=1e-3, weight_decay=0.01)
+        opt = oracle.RefAdamW(ps, gs, lr=1e-3, weight_decay=0.01)
         kind = "reference"
 
         def one():
@@ -104,11 +135,11 @@ def cpu_reference_sample(n: int, steps: int, warmup: int = 1) -> dict:
             opt.step()
     else:
         cfg = oracle.StepConfig(layout=0, max_norm=1.0)
-        opt = oracle.PortOptimizer([p], [0.01], cfg)
+        opt = oracle.PortOptimizer(ps, [0.01] * len(ps), cfg)
         kind = "port"
 
         def one():
-            opt.step([g])
+            opt.step(gs)
     for _ in range(warmup):
         one()
     t0 = time.perf_counter()
@@ -116,38 +147,40 @@ def cpu_reference_sample(n: int, steps: int, warmup: int = 1) -> dict:
         one()
     dt = time.perf_counter() - t0
     return {"value": n * steps / dt / 1e9, "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{steps} steps of clip_grad_norm(1.0)+step() on one fp32 bucket of "
-                      f"{n} params (host arrays, unscale/bf16 cast not timed)",
-            "ms_per_step": dt / steps * 1e3}
+            "sample": f"{steps} steps (after {warmup} warm-up) of clip_grad_norm(1.0)+step() on "
+                      f"{n} fp32 params in {len(sizes)} buckets (host arrays; the unscale and "
+                      "bf16 cast, which the reference lacks, not timed)",
+            "ms_per_step": dt / steps * 1e3, "params": n}
 
 
-def cpu_single_thread_sample(n: int, steps: int = 3) -> dict | None:
-    """The same sample on one host thread, in a child process (OpenMP reads
-    OMP_NUM_THREADS when the library starts)."""
-    env = dict(os.environ, OMP_NUM_THREADS="1")
+def cpu_child(n: int, steps: int, warmup: int, threads: int, timeout: float = 900) -> dict:
+    """cpu_reference_sample in a fresh child process with OMP_NUM_THREADS set
+    before any OpenMP runtime starts (a torchrun parent sets it to 1)."""
+    env = dict(os.environ, OMP_NUM_THREADS=str(threads))
     r = subprocess.run([sys.executable, str(Path(__file__).resolve()), "--cpu-sample",
-                        "--params", str(n), "--steps", str(steps)],
-                       env=env, capture_output=True, text=True, timeout=300)
+                        "--params", str(n), "--steps", str(steps), "--warmup", str(warmup)],
+                       env=env, capture_output=True, text=True, timeout=timeout)
     lines = [x for x in r.stdout.splitlines() if x.startswith("{")]
     if r.returncode != 0 or not lines:
-        return None
-    d = json.loads(lines[-1])
-    return {"value": d["value"], "cores": d["cores"], "sample": d["sample"]}
+        raise RuntimeError(f"CPU reference child failed ({r.returncode}): {r.stderr[-400:]}")
+    return json.loads(lines[-1])
 
 
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    n = min(BUCKET, args.params)
     t0 = time.perf_counter()
-    res = cpu_reference_sample(n, args.steps, args.warmup)
+    threads = host_threads()
+    res = cpu_child(args.params, args.steps, args.warmup, threads)
     line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config4 sample: one 25M bucket, fp32 reference AdamW",
-                       "params": n},
+            "config": {"workload": "config4 on the host: the reference's clip_grad_norm(1.0) + "
+                                   "step() over 200M fp32 params in 25M buckets",
+                       "params": args.params, "bucket": BUCKET, "same_config": True,
+                       "threads": threads},
             "cpu_baseline": {k: res[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
@@ -421,12 +454,7 @@ def run_ours(args):
     if comm:
         torch.distributed.all_reduce(ph, op=torch.distributed.ReduceOp.MAX)
     phases = {k: round(float(v), 4) for k, v in zip(phase_names, ph.tolist())}
-    nvl = None
-    if fused:
-        try:  # a reported roofline, never a reason to lose the bench line
-            nvl = nvlink_rates(torch, world, rank, local, 2 * shard_params, phases)
-        except Exception as ex:
-            nvl = {"error": str(ex)[:300]}
+    probe = nvlink_probe_rates(torch, world, rank, local, 2 * shard_params) if fused else None
     if apply_ms is None:  # device-synchronised step: the update phase of the loop above
         apply_ms = [float(ph[phase_names.index("update+allgather")])]
     t = torch.tensor([ms, statistics.mean(apply_ms)], dtype=torch.float64, device=dev)
@@ -438,46 +466,63 @@ def run_ours(args):
     # ---- end to end through the public API with host buffers -------------
     g_pin = torch.from_numpy(g_host.view(np.int16)).view(torch.bfloat16).pin_memory()
     p_pin = torch.empty(n, dtype=torch.bfloat16).pin_memory()
-    barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
     # the step's result read back: each rank's own updated shard of the bf16
     # params (the ranks' shards together are the whole model once; at N = 1
     # the whole model)
     own = [(b.own_start, b.own_size) for b in z.buckets if b.own_size > 0]
-    for _ in range(args.e2e_steps):
-        grads.copy_(g_pin, non_blocking=True)
-        z.step()
-        for lo, sz in own:
-            p_pin[lo:lo + sz].copy_(params[lo:lo + sz], non_blocking=True)
-    e1.record(stream)
+    barrier()
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
+    e2e_ms = e2e_overlapped(torch, z.step, stream, grads, params, g_pin, p_pin, own,
+                            args.e2e_steps)
     t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
     if comm:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     e2e_ms = float(t[0])
 
+    # ---- parity of one more step: oracle replay on rank 0, identity on all --
+    barrier()
+    torch.cuda.synchronize()
+    parity = parity_check(torch, np, z, world, rank, comm, g_pin, grads, params)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            cpu = cpu_reference_sample(min(BUCKET, n), 5)
+            cpu = cpu_child(BUCKET, 5, 1, host_threads())
             cpu.pop("ms_per_step", None)
-            cpu["single_thread"] = cpu_single_thread_sample(min(BUCKET, n) // 5)
+            cpu.pop("params", None)
+            one = cpu_child(BUCKET // 5, 3, 1, 1)
+            cpu["single_thread"] = {"value": one["value"], "cores": one["cores"],
+                                    "sample": one["sample"]}
         except Exception as ex:  # the baseline is reported, never required
-            cpu = {"error": str(ex)}
+            cpu = {"error": str(ex)[:300]}
 
     if fused:
         z.close()
+    del z
     if comm:
         torch.distributed.barrier(device_ids=[local])
         torch.distributed.destroy_process_group()
+    torch.cuda.empty_cache()
+    peak, peak_kind = measured_peak_hbm()
+    configs = None
+    if rank == 0 and world == 1 and not args.no_configs:
+        try:
+            configs = measure_configs(torch, peak, steps=20)
+        except Exception as ex:  # reported beside the headline, never a reason to lose it
+            configs = {"error": str(ex)[:300]}
     if rank != 0:
         return 0
-    peak, peak_kind = measured_peak_hbm()
     apply_bytes = BYTES_PER_PARAM * shard_params
     achieved = apply_bytes / (apply_ms_max * 1e-3) / 1e9
+    hbm = {"bound": "hbm", "kernel": "k_apply", "achieved": achieved, "peak": peak,
+           "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+           "traffic": APPLY_TRAFFIC_BYTES.get(shard_params),
+           "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_apply "
+                             "launch of this command at N=1" if shard_params in
+                             APPLY_TRAFFIC_BYTES else None,
+           "algorithmic_bytes_per_launch": apply_bytes, "apply_ms": apply_ms_max}
+    roofline = hbm if world == 1 else nvlink_roofline(world, shard_params, phases,
+                                                      ms_max / args.steps)
     units = world * n * args.steps
     line = {
         "metric": METRIC,
@@ -504,33 +549,235 @@ def run_ours(args):
                    "global_batch": None, "seq_len": None,
                    "l2": "inputs larger than L2 (16 B/param resident state = "
                          f"{16 * shard_params / 1e9:.1f} GB per rank)"},
-        "roofline": {"bound": "hbm", "kernel": "k_apply", "achieved": achieved, "peak": peak,
-                     "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": APPLY_TRAFFIC_BYTES.get(shard_params),
-                     "algorithmic_bytes_per_launch": apply_bytes,
-                     "apply_ms": apply_ms_max},
+        "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": {"value": world * n * args.e2e_steps / (e2e_ms * 1e-3) / 1e9, "unit": UNIT,
                 "h2d_bytes_per_step": 2 * n, "d2h_bytes_per_step": 2 * shard_params,
                 "transfers": "per rank: H2D of its full bf16 gradient from pinned memory, D2H "
-                             "of its updated shard of the bf16 params",
-                "ms_per_step": e2e_ms / args.e2e_steps},
+                             "of its updated shard of the bf16 params; read-back of step s "
+                             "overlaps the upload of step s+1 (two copy streams)",
+                "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps},
         "clocks": clock_info,
         "gpu_launches": launches_per_step * args.steps,
         "phases_ms": phases,
-        "nvlink": nvl,
+        "parity": parity,
         "final_info": {"step": info.step, "skipped": info.skipped, "loss_scale": info.loss_scale,
                        "grad_norm": info.grad_norm},
     }
+    if world > 1:
+        line["roofline_hbm"] = hbm
+        line["nvlink_probe"] = probe
+    if configs is not None:
+        line["configs"] = configs
     print(json.dumps(line), flush=True)
     return 0
 
 
-def nvlink_rates(torch, world, rank, local, shard_bytes, phases):
-    """The fused kernels' NVLink rates against the raw rates of their access
-    patterns on this box (soar_nvlink_probe: all ranks at once, no arithmetic,
-    the same bytes per peer as the step). GB/s per direction per rank; max
-    time over ranks."""
+def e2e_overlapped(torch, step, stream, grads, params, g_pin, p_pin, own, steps) -> float:
+    """`steps` steps through the public API with host buffers, timed on
+    `stream` with CUDA events. Step s: H2D of the gradient on one copy stream
+    once step s-1 has consumed the previous one; the step on `stream` once the
+    upload has landed and the read-back of step s-1 has left the parameter
+    buffer; D2H of the updated params on a second copy stream. Both PCIe
+    directions run at once (the read-back of step s beside the upload of step
+    s+1). Returns ms for all steps."""
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    up = [torch.cuda.Event() for _ in range(steps)]
+    done = [torch.cuda.Event() for _ in range(steps)]
+    back = [torch.cuda.Event() for _ in range(steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(steps):
+        h2d.wait_event(done[s - 1] if s else e0)
+        with torch.cuda.stream(h2d):
+            grads.copy_(g_pin, non_blocking=True)
+        up[s].record(h2d)
+        stream.wait_event(up[s])
+        if s:
+            stream.wait_event(back[s - 1])
+        step()
+        done[s].record(stream)
+        d2h.wait_event(done[s])
+        with torch.cuda.stream(d2h):
+            for lo, sz in own:
+                p_pin[lo:lo + sz].copy_(params[lo:lo + sz], non_blocking=True)
+        back[s].record(d2h)
+    stream.wait_event(back[steps - 1])
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def parity_check(torch, np, z, world, rank, comm, g_pin, grads, params) -> dict:
+    """One more step after the timed work, checked three ways (every rank runs
+    the same collectives):
+      params_identical  a checksum of every rank's full bf16 parameter buffer
+                        agrees across ranks;
+      counters_equal    (step, skipped, loss scale, growth tracker, norm bits)
+                        agree across ranks and with the oracle;
+      sampled replay    the oracle (oracle/, the port of the reference's
+                        src/optim/adamw.cpp:28-117 plus the loss scaler)
+                        replays the step on ~65536 seeded elements of rank 0's
+                        shard from its state before the step and the averaged
+                        gradient the step consumed; master/m/v and the bf16
+                        params are compared with the device.
+    The reduce is compared with the oracle's rank-ordered reduce of the R raw
+    gradients on the same sample, and the device's global norm with an fp64
+    norm of the averaged gradients computed independently with torch."""
+    import torch.distributed as tdist
+
+    from oracle import oracle
+    from soar_b200.dp import plan_buckets
+    dev = grads.device
+    out = {"sample": 0, "checked_rank": 0}
+    try:
+        # rank 0's tensors (its owned slices, in bucket order) and a seeded sample
+        b0 = [b for b in plan_buckets(z.n, BUCKET, world, 0) if b.own_size > 0]
+        rng = np.random.Generator(np.random.PCG64(20260))
+        per = max(1, 65536 // max(1, len(b0)))
+        picks = []  # (k-th tensor of rank 0, offset)
+        for k, b in enumerate(b0):
+            offs = np.unique(np.concatenate([rng.integers(0, b.own_size, per),
+                                             [0, b.own_size - 1]]))
+            picks.extend((k, int(o)) for o in offs)
+        flat = torch.tensor([b0[k].own_start + o for k, o in picks], dtype=torch.int64,
+                            device=dev)
+        out["sample"] = len(picks)
+        by_t = {}
+        for k, o in picks:
+            by_t.setdefault(k, []).append(o)
+
+        def sample_state(kind):
+            nz = [i for i, sg in enumerate(z.shard_grads) if sg.numel() > 0]
+            return np.concatenate([z.opt.state(nz[k], kind)[torch.tensor(by_t[k], device=dev)]
+                                   .cpu().numpy() for k in sorted(by_t)])
+
+        # fresh raw gradients on every rank, and their values on rank 0's sample
+        grads.copy_(g_pin)
+        torch.cuda.synchronize()
+        raw = grads.view(torch.int16)[flat].contiguous()
+        raws = [raw]
+        if world > 1:
+            raws = [torch.empty_like(raw) for _ in range(world)]
+            tdist.all_gather(raws, raw)
+        info_b = z.opt.info()
+        if rank == 0:
+            st = {key: sample_state(kind) for kind, key in ((0, "master"), (1, "m"), (2, "v"))}
+            p_before = params.view(torch.int16)[flat].cpu().numpy().view(np.uint16)
+        torch.cuda.synchronize()
+        if comm:
+            tdist.barrier()
+        z.step()
+        torch.cuda.synchronize()
+        info = z.opt.info()
+        # the averaged gradient the step consumed (in place in the own slices
+        # for the fused reduce-scatter, the shard buffer for NCCL): an
+        # independent fp64 norm over every rank's shard
+        ss = torch.zeros(1, dtype=torch.float64, device=dev)
+        for sg in z.shard_grads:
+            if sg.numel():
+                ss += ((sg.to(torch.float64) / info_b.loss_scale) ** 2).sum()
+        if world > 1:
+            tdist.all_reduce(ss)
+        norm64 = float(torch.sqrt(ss)[0])
+        out["norm_rel_err_vs_fp64"] = abs(info.grad_norm - norm64) / max(norm64, 1e-30)
+        # identity across ranks
+        w = params.view(torch.int32).to(torch.int64)
+        pos = torch.arange(w.numel(), device=dev, dtype=torch.int64) % 65521 + 1
+        cks = torch.stack([w.sum(), ((w & 0xFFFFFFFF) * pos).sum()])
+        del w, pos
+        bits = lambda x: int(np.float32(x).view(np.int32))
+        cnt = torch.tensor([info.step, info.skipped, bits(info.loss_scale), info.growth_tracker,
+                            bits(info.grad_norm)], dtype=torch.int64, device=dev)
+        all_cks, all_cnt = [cks], [cnt]
+        if world > 1:
+            all_cks = [torch.empty_like(cks) for _ in range(world)]
+            all_cnt = [torch.empty_like(cnt) for _ in range(world)]
+            tdist.all_gather(all_cks, cks)
+            tdist.all_gather(all_cnt, cnt)
+        out["params_identical"] = all(bool(torch.equal(c, all_cks[0])) for c in all_cks)
+        counters_same = all(bool(torch.equal(c, all_cnt[0])) for c in all_cnt)
+        if rank != 0:
+            return out
+        nz = [i for i, sg in enumerate(z.shard_grads) if sg.numel() > 0]
+        avg = np.concatenate([z.shard_grads[nz[k]][torch.tensor(by_t[k], device=dev)]
+                              .view(torch.int16).cpu().numpy().view(np.uint16)
+                              for k in sorted(by_t)])
+        raw_np = [r.cpu().numpy().view(np.uint16) for r in raws]
+        red = oracle.reduce_avg_bf16(raw_np) if world > 1 else raw_np[0]
+        out["reduce_bit_exact"] = bool(np.array_equal(red, avg))
+        out["reduce_max_ulp"] = int(np.abs(red.astype(np.int32) - avg.astype(np.int32)).max())
+        # the oracle's step on the sample, from the device's state before it
+        cfg = oracle.StepConfig(layout=1, lr=1e-3, max_norm=1.0, use_scaler=True)
+        ps = oracle.PortShard([p_before.copy()], [avg.copy()], [0.01], cfg,
+                              init_scale=info_b.loss_scale)
+        ps.master[0][:] = st["master"]
+        ps.m[0][:] = st["m"]
+        ps.v[0][:] = st["v"]
+        ps.state.t, ps.state.skipped = info_b.step, info_b.skipped
+        ps.state.tracker = info_b.growth_tracker
+        norm = np.float64(np.float32(info.grad_norm))
+        ps.apply_sumsq(float(norm * norm))  # the square of a float is exact: same fp32 norm
+        got_p = params.view(torch.int16)[flat].cpu().numpy().view(np.uint16)
+        got = {key: sample_state(kind) for kind, key in ((0, "master"), (1, "m"), (2, "v"))}
+        want = {"master": ps.master[0], "m": ps.m[0], "v": ps.v[0]}
+        rel, exact = 0.0, True
+        for k in want:
+            a, b = got[k].astype(np.float64), want[k].astype(np.float64)
+            rel = max(rel, float(np.max(np.abs(a - b) / np.maximum(np.abs(b), 1e-30))))
+            exact = exact and bool(np.array_equal(got[k].view(np.uint32),
+                                                  want[k].view(np.uint32)))
+        out["max_ulp"] = int(np.abs(got_p.astype(np.int32) - ps.params[0].astype(np.int32)).max())
+        out["state_max_rel_err"] = rel
+        out["state_bit_exact"] = exact
+        oc = (ps.state.t, ps.state.skipped, float(ps.state.scale), ps.state.tracker)
+        dc = (info.step, info.skipped, float(info.loss_scale), info.growth_tracker)
+        out["counters_equal"] = counters_same and oc == dc
+        out["tolerance"] = "bf16 params <= 1 ulp; fp32 state max rel err <= 1e-6"
+        out["pass"] = bool(out["params_identical"] and out["counters_equal"] and
+                           out["max_ulp"] <= 1 and rel <= 1e-6 and
+                           out["norm_rel_err_vs_fp64"] <= 1e-6)
+    except Exception as ex:  # reported, never a reason to lose the bench line
+        out["error"] = f"{type(ex).__name__}: {str(ex)[:300]}"
+    return out
+
+
+def nvlink_roofline(world, shard_params, phases, ms_per_step) -> dict:
+    """The binding roofline at N > 1: NVLink. Per step each rank pulls its
+    shard of every peer's gradient ((R-1) x shard x 2 B in, and as much out
+    while the peers pull theirs) and pushes its updated bf16 shard into every
+    peer ((R-1) x shard x 2 B out, as much in): 2 (R-1)/R x 2N bytes per
+    direction per rank. `achieved` divides them by the two collective phases'
+    times (phases_ms); `step_gbs` by the whole step."""
+    per_kernel = (world - 1) * shard_params * 2
+    nbytes = 2 * per_kernel
+    if "update+allgather" in phases:
+        t_rs, t_ag = phases["reduce_scatter+sumsq"], phases["update+allgather"]
+        kernels = "k_rs_sumsq + k_apply<all-gather>"
+    else:
+        t_rs, t_ag = phases["reduce_scatter"], phases["update"] + phases["param_allgather"]
+        kernels = "NCCL reduce-scatter + k_apply + NCCL all-gather"
+    achieved = nbytes / ((t_rs + t_ag) * 1e-3) / 1e9
+    step_gbs = nbytes / (ms_per_step * 1e-3) / 1e9
+    return {"bound": "nvlink", "kernel": kernels, "unit": "GB/s per direction per rank",
+            "achieved": achieved, "peak": NVLINK_PEER_COPY_GBS,
+            "peak_kind": "measured peer copy of this pool (per direction per GPU)",
+            "frac": achieved / NVLINK_PEER_COPY_GBS,
+            "peak_spec": NVLINK_SPEC_GBS, "frac_spec": achieved / NVLINK_SPEC_GBS,
+            "bytes_per_step": nbytes, "bytes_per_launch": per_kernel,
+            "phase_ms": {"reduce": t_rs, "update": t_ag},
+            "step_gbs": step_gbs, "step_frac": step_gbs / NVLINK_PEER_COPY_GBS,
+            "traffic": None,
+            "formula": "achieved = 2 x (R-1) x shard x 2 B / (reduce + update phase ms)"}
+
+
+def nvlink_probe_rates(torch, world, rank, local, shard_bytes) -> dict:
+    """Raw rates of the fused kernels' two peer access patterns on this box
+    (the bench-only probe library: all ranks at once, no arithmetic, the same
+    bytes per peer as the step). GB/s per direction per rank; max time over
+    ranks. A failure on any rank is agreed on by every rank before the next
+    collective, so the ranks never run different collectives, and the buffers
+    are released whatever happens."""
     import ctypes as C
 
     import torch.distributed as dist
@@ -539,69 +786,197 @@ def nvlink_rates(torch, world, rank, local, shard_bytes, phases):
     lib = _o.lib()
     tile_lcm = 64 * 1024
     bpp = max(tile_lcm, shard_bytes // tile_lcm * tile_lcm)
+    dev = f"cuda:{local}"
+    err = None
+
+    def agree(ok: bool) -> bool:
+        f = torch.tensor([0 if ok else 1], dtype=torch.int32, device=dev)
+        dist.all_reduce(f, op=dist.ReduceOp.MAX)
+        return int(f.item()) == 0
+
     ptr = C.c_void_p()
     handle = (C.c_ubyte * _o.IPC_HANDLE_BYTES)()
-    _o._check(lib.soar_ipc_alloc(world * bpp, local, C.byref(ptr), handle), "soar_ipc_alloc")
-    handles = [None] * world
-    dist.all_gather_object(handles, bytes(handle))
-    bases, opened = [], []
-    for q, h in enumerate(handles):
-        if q == rank:
-            bases.append(ptr.value)
+    opened = []
+    allocated = False
+    try:
+        probe = None
+        try:
+            probe = _o.probe_lib()
+            _o._check(lib.soar_ipc_alloc(world * bpp, local, C.byref(ptr), handle),
+                      "soar_ipc_alloc")
+            allocated = True
+            ok = True
+        except Exception as ex:
+            err, ok = str(ex)[:200], False
+        if not agree(ok):
+            return {"error": err or "failed on another rank"}
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle))
+        bases = []
+        try:
+            for q, h in enumerate(handles):
+                if q == rank:
+                    bases.append(ptr.value)
+                    continue
+                peer = C.c_void_p()
+                buf = (C.c_ubyte * _o.IPC_HANDLE_BYTES).from_buffer_copy(h)
+                _o._check(lib.soar_ipc_open(buf, local, C.byref(peer)), "soar_ipc_open")
+                bases.append(peer.value)
+                opened.append(peer.value)
+            ok = True
+        except Exception as ex:
+            err, ok = str(ex)[:200], False
+        if not agree(ok):
+            return {"error": err or "failed on another rank"}
+        arr = (C.c_void_p * world)(*bases)
+        d_err = torch.zeros(1, dtype=torch.int32, device=dev)
+        stream = torch.cuda.current_stream()
+        sms = torch.cuda.get_device_properties(local).multi_processor_count
+        failed = [False]
+
+        def launch(mode, tile, stages, grid):
+            if failed[0]:
+                return  # the collectives below still run: every rank takes the same steps
+            rc = probe.soar_nvlink_probe(arr, world, rank, bpp, mode, tile, stages, grid,
+                                         C.c_void_p(d_err.data_ptr()),
+                                         C.c_void_p(stream.cuda_stream))
+            failed[0] = rc != 0
+
+        def timed(mode, tile, stages, grid, reps=5):
+            for _ in range(2):
+                launch(mode, tile, stages, grid)
+            torch.cuda.synchronize()
+            dist.barrier(device_ids=[local])
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(reps):
+                launch(mode, tile, stages, grid)
+            b.record(stream)
+            torch.cuda.synchronize()
+            t = torch.tensor([a.elapsed_time(b) / reps], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return round((world - 1) * bpp / (float(t[0]) * 1e-3) / 1e9, 1)
+
+        pull = {f"tile{tile}_stages{st}_grid{g}": timed(0, tile, st, g)
+                for tile, st, g in ((4096, 4, sms), (2048, 8, 2 * sms))
+                if st * tile * (world - 1) <= 200 * 1024}
+        push = {f"tile{tile}_grid{g}": timed(1, tile, 0, g)
+                for tile, g in ((2048, 2 * sms), (8192, sms))}
+        torch.cuda.synchronize()
+        if not agree(not failed[0] and int(d_err.item()) == 0):
+            return {"error": "a probe launch failed or a wait timed out on some rank"}
+        return {"unit": "GB/s per direction per rank, all ranks at once",
+                "bytes_per_peer": bpp, "pull": pull, "push": push}
+    finally:
+        torch.cuda.synchronize()
+        for pp in opened:
+            lib.soar_ipc_close(C.c_void_p(pp), local)
+        dist.barrier(device_ids=[local])  # no rank frees while a peer still maps it
+        if allocated:
+            lib.soar_ipc_free(ptr, local)
+
+
+# ----------------------------------------------------------- configs 1-3, 5 --
+
+def config_specs(sizes5=(1_000_000, 16_000_000, 256_000_000)):
+    """BASELINE configs at their own shapes:
+      c1  1 fp32 tensor of 1,048,576 params, no clip/scaler, wd 0.01;
+      c2  the 240-tensor segmentation-net list (~12M fp32), wd 0.05 on conv
+          weights / 0 on norms and biases, cosine 1e-3 -> 1e-5 over 100 steps
+          (the scheduler steps after every step, on the host);
+      c3  400 bf16-mixed tensors summing to 50M, clip 1.0, loss scaler 65536;
+      c5  one flat tensor of N params in both layouts, plain update."""
+    import math
+
+    from soar_b200 import synth
+    c2_shapes = synth.config2_shapes()
+    specs = {
+        "c1": dict(sizes=[1_048_576], wd=[0.01], layout="fp32", clip=0.0, scaler=False,
+                   cosine=None),
+        "c2": dict(sizes=[int(math.prod(sh)) for _, sh in c2_shapes],
+                   wd=[0.05 if k in ("dw", "pw") else 0.0 for k, _ in c2_shapes],
+                   layout="fp32", clip=0.0, scaler=False, cosine=(100, 1e-5, 0)),
+        "c3": dict(sizes=synth.config3_sizes(), wd=None, layout="bf16_mixed", clip=1.0,
+                   scaler=True, cosine=None),
+    }
+    for n in sizes5:
+        for lay, tag in (("fp32", "fp32"), ("bf16_mixed", "mixed")):
+            specs[f"c5_{tag}_{n // 1_000_000}M"] = dict(sizes=[n], wd=[0.01], layout=lay,
+                                                        clip=0.0, scaler=False, cosine=None)
+    return specs
+
+
+def measure_configs(torch, peak: float, steps: int = 20, names=None) -> dict:
+    """Each config: 3 warm-up steps, then `steps` steps, each timed alone with
+    CUDA events after a 256 MB L2 flush (so no step reads the previous step's
+    data from L2). Inputs are device-generated; the numerics of these configs
+    are pinned by the parity tests. Returns {name: figures}."""
+    import soar_b200 as sb
+    specs = config_specs()
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    out = {}
+    for name, c in specs.items():
+        if names and name not in names:
             continue
-        peer = C.c_void_p()
-        buf = (C.c_ubyte * _o.IPC_HANDLE_BYTES).from_buffer_copy(h)
-        _o._check(lib.soar_ipc_open(buf, local, C.byref(peer)), "soar_ipc_open")
-        bases.append(peer.value)
-        opened.append(peer.value)
-    arr = (C.c_void_p * world)(*bases)
-    err = torch.zeros(1, dtype=torch.int32, device=f"cuda:{local}")
-    stream = torch.cuda.current_stream()
-    sms = torch.cuda.get_device_properties(local).multi_processor_count
-    gbs = lambda ms: (world - 1) * bpp / (ms * 1e-3) / 1e9
+        dt = torch.bfloat16 if c["layout"] == "bf16_mixed" else torch.float32
+        ps = [(torch.randn(k, device="cuda") * 0.02).to(dt) for k in c["sizes"]]
+        gs = [(torch.randn(k, device="cuda") * (1e-3 * (65536.0 if c["scaler"] else 1.0))).to(dt)
+              for k in c["sizes"]]
+        wds = c["wd"] or [0.01] * len(ps)
+        groups = [sb.ParamGroup([p], w) for p, w in zip(ps, wds)]
+        opt = sb.AdamW(groups, sb.AdamWOptions(lr=1e-3), layout=c["layout"],
+                       max_grad_norm=c["clip"],
+                       loss_scaler=sb.LossScalerOptions(init_scale=65536.0) if c["scaler"]
+                       else None, grads=gs)
+        sched = sb.CosineAnnealingLR(opt, *c["cosine"]) if c["cosine"] else None
+        s = torch.cuda.Stream()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(steps)]
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                opt.step(s)
+            for a, b in evs:
+                flush.fill_(1.0)
+                a.record(s)
+                opt.step(s)
+                b.record(s)
+                if sched:
+                    sched.step()
+        torch.cuda.synchronize()
+        us = [a.elapsed_time(b) * 1e3 for a, b in evs]
+        n = sum(c["sizes"])
+        mean_us = statistics.mean(us)
+        gbs = BYTES_PER_PARAM * n / (mean_us * 1e-6) / 1e9
+        info = opt.info()
+        out[name] = {"params": n, "tensors": len(c["sizes"]), "layout": c["layout"],
+                     "us_per_step": round(mean_us, 2), "us_median": round(statistics.median(us), 2),
+                     "gparams_s": round(n / (mean_us * 1e-6) / 1e9, 2),
+                     "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 3),
+                     "steps": steps, "final_step": info.step, "skipped": info.skipped}
+        if sched:
+            sched.close()
+        opt.close()
+        del ps, gs, opt
+        torch.cuda.empty_cache()
+    out["_how"] = (f"each step timed alone (CUDA events) after an L2 flush "
+                   f"({L2_FLUSH_BYTES >> 20} MB write), 3 warm-up steps; frac of the measured "
+                   f"{peak:.0f} GB/s HBM copy at 28 B/param")
+    return out
 
-    def timed(mode, tile, stages, grid, reps=5):
-        def launch():
-            _o._check(lib.soar_nvlink_probe(arr, world, rank, bpp, mode, tile, stages, grid,
-                                            C.c_void_p(err.data_ptr()),
-                                            C.c_void_p(stream.cuda_stream)), "soar_nvlink_probe")
-        for _ in range(2):
-            launch()
-        torch.cuda.synchronize()
-        dist.barrier(device_ids=[local])
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for _ in range(reps):
-            launch()
-        b.record(stream)
-        torch.cuda.synchronize()
-        t = torch.tensor([a.elapsed_time(b) / reps], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return round(gbs(float(t[0])), 1)
 
-    pull = {f"tile{tile}_stages{st}_grid{g}": timed(0, tile, st, g)
-            for tile, st, g in ((4096, 4, sms), (2048, 8, 2 * sms))
-            if st * tile * (world - 1) <= 200 * 1024}
-    push = {f"tile{tile}_grid{g}": timed(1, tile, 0, g)
-            for tile, g in ((2048, 2 * sms), (8192, sms))}
-    torch.cuda.synchronize()
-    failed = int(err.item())
-    dist.barrier(device_ids=[local])
-    for pp in opened:
-        lib.soar_ipc_close(C.c_void_p(pp), local)
-    dist.barrier(device_ids=[local])
-    lib.soar_ipc_free(ptr, local)
-    rs = (world - 1) * shard_bytes / (phases["reduce_scatter+sumsq"] * 1e-3) / 1e9
-    ag = (world - 1) * shard_bytes / (phases["update+allgather"] * 1e-3) / 1e9
-    p_pull, p_push = max(pull.values()), max(push.values())
-    return {"unit": "GB/s per direction per rank", "bytes_per_peer": shard_bytes,
-            "k_rs_sumsq": {"achieved": round(rs, 1), "peak": p_pull, "frac": round(rs / p_pull, 3),
-                           "peak_kind": "measured: soar_nvlink_probe pull, all ranks at once"},
-            "k_apply_allgather": {"achieved": round(ag, 1), "peak": p_push,
-                                  "frac": round(ag / p_push, 3),
-                                  "peak_kind": "measured: soar_nvlink_probe push, all ranks at once"},
-            "probe": {"pull": pull, "push": push, "wait_error": failed}}
+def run_configs(args):
+    """BASELINE configs 1-3 and the config-5 sizes on one GPU, one JSON line
+    each (see measure_configs)."""
+    import torch
+    torch.cuda.set_device(0)
+    peak, peak_kind = measured_peak_hbm()
+    res = measure_configs(torch, peak, steps=args.steps)
+    how = res.pop("_how")
+    for name, r in res.items():
+        print(json.dumps({"config": name, "metric": "AdamW Gparams/s (BASELINE configs)",
+                          "peak_kind": peak_kind, "how": how, **r}), flush=True)
+    return 0
 
 
 def run_sweep(args):
@@ -713,84 +1088,10 @@ def run_sweep(args):
     return 0
 
 
-def run_configs(args):
-    """BASELINE configs 1-3 at their own shapes on one GPU, K steps back to back
-    through the API after 3 warm-up, one JSON line each: Gparams/s, step ms and
-    k_apply-equivalent GB/s (28 B/param) against the measured HBM copy.
-      c1  1 fp32 tensor of 1,048,576 params, no clip/scaler;
-      c2  the 240-tensor segmentation-net list (~12M fp32), wd 0.05 on conv
-          weights / 0 on norms and biases, cosine 1e-3 -> 1e-5 over 100 steps
-          (the scheduler steps after every step, on the host);
-      c3  400 bf16-mixed tensors summing to 50M, clip 1.0, loss scaler 65536.
-    Inputs are device-generated; the numerics of these configs are pinned by
-    the parity tests, not here."""
-    import math
-
-    import torch
-
-    import soar_b200 as sb
-    from soar_b200 import synth
-    torch.cuda.set_device(0)
-    peak, peak_kind = measured_peak_hbm()
-
-    def rnd(n, std, dt):
-        return (torch.randn(n, device="cuda") * std).to(dt)
-
-    c2_shapes = synth.config2_shapes()
-    cfgs = {
-        "c1": dict(sizes=[1_048_576], wd=[0.01], layout="fp32", clip=0.0, scaler=None,
-                   cosine=None),
-        "c2": dict(sizes=[int(math.prod(sh)) for _, sh in c2_shapes],
-                   wd=[0.05 if k in ("dw", "pw") else 0.0 for k, _ in c2_shapes],
-                   layout="fp32", clip=0.0, scaler=None, cosine=(100, 1e-5, 0)),
-        "c3": dict(sizes=synth.config3_sizes(), wd=None, layout="bf16_mixed", clip=1.0,
-                   scaler=sb.LossScalerOptions(init_scale=65536.0), cosine=None),
-    }
-    for name, c in cfgs.items():
-        dt = torch.bfloat16 if c["layout"] == "bf16_mixed" else torch.float32
-        ps = [rnd(n, 0.02, dt) for n in c["sizes"]]
-        gs = [rnd(n, 1e-3 * (65536.0 if c["scaler"] else 1.0), dt) for n in c["sizes"]]
-        wds = c["wd"] or [0.01] * len(ps)
-        groups = [sb.ParamGroup([p], w) for p, w in zip(ps, wds)]
-        opt = sb.AdamW(groups, sb.AdamWOptions(lr=1e-3), layout=c["layout"],
-                       max_grad_norm=c["clip"], loss_scaler=c["scaler"], grads=gs)
-        sched = sb.CosineAnnealingLR(opt, *c["cosine"]) if c["cosine"] else None
-        s = torch.cuda.Stream()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(s):
-            for _ in range(3):
-                opt.step(s)
-            torch.cuda.synchronize()
-            a.record(s)
-            for _ in range(args.steps):
-                opt.step(s)
-                if sched:
-                    sched.step()
-            b.record(s)
-        torch.cuda.synchronize()
-        ms = a.elapsed_time(b) / args.steps
-        n = sum(c["sizes"])
-        gbs = BYTES_PER_PARAM * n / (ms * 1e-3) / 1e9
-        info = opt.info()
-        print(json.dumps({"config": name, "metric": "AdamW Gparams/s (BASELINE configs 1-3)",
-                          "params": n, "tensors": len(c["sizes"]), "layout": c["layout"],
-                          "steps": args.steps, "warmup": 3, "ms_per_step": ms,
-                          "value": n / (ms * 1e-3) / 1e9, "unit": "Gparams/s",
-                          "achieved_gbs": gbs, "peak_gbs": peak, "peak_kind": peak_kind,
-                          "frac": gbs / peak, "final_step": info.step,
-                          "skipped": info.skipped}), flush=True)
-        if sched:
-            sched.close()
-        opt.close()
-        del ps, gs, opt
-        torch.cuda.empty_cache()
-    return 0
-
-
 def main():
     args = parse()
     if args.cpu_sample:
-        res = cpu_reference_sample(args.params, args.steps)
+        res = cpu_reference_sample(args.params, args.steps, args.warmup)
         print(json.dumps(res), flush=True)
         return 0
     if args.impl == "reference":

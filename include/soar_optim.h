@@ -3,7 +3,7 @@
  *
  * Drop-in for the update step of pomagrenate/soar.cpp: the reference's
  * soar::optim::AdamW / CosineAnnealingLR (include/soar/optim/adamw.hpp:10-57,
- * src/optim/adamw.cpp:66-202), which the Trainer calls as
+ * src/optim/adamw.cpp:7-143), which the Trainer calls as
  * clip_grad_norm(grad_clip) -> step() -> zero_grad()
  * (src/engine/trainer.cpp:157-159, 223-225). The reference exposes its engine
  * through an opaque-handle C-ABI (include/soar/api/c_api.h) bound from Python
@@ -11,7 +11,7 @@
  * conventions and are additive to it:
  *   - SOAR_API = default visibility (c_api.h:10-14);
  *   - opaque void* handles; int status, 0 = success, -1 = any failure or NULL
- *     argument (src/api/c_api.cpp:82-84, 100, 129, 148);
+ *     argument (src/api/c_api.cpp:51, 80, 99-100, 143, 149-150);
  *   - caller-owned out-pointers;
  *   - plus a `void* stream` (a cudaStream_t; NULL = legacy default stream), the
  *     convention of the reference's kernel API (include/soar/cuda/cuda_kernels.hpp:108-127).
@@ -49,7 +49,7 @@ extern "C" {
 /* Storage layouts. 28 algorithmic bytes per parameter per step in both. */
 enum soar_layout {
     /* fp32 params (updated in place, they are the master), fp32 grads, fp32 m/v:
-       the reference's only layout (adamw.cpp:143-147). */
+       the reference's only layout (adamw.cpp:84-88). */
     SOAR_LAYOUT_FP32 = 0,
     /* bf16 params and grads, fp32 master/m/v owned by the optimizer; params are
        rewritten as round-to-nearest-even bf16 of the master every step. */
@@ -68,7 +68,7 @@ enum soar_state_kind {
 typedef struct soar_tensor_desc {
     void* param;        /* device; fp32 (FP32 layout) or bf16 (BF16_MIXED) */
     void* grad;         /* device, same dtype as param. NULL: the tensor is skipped by
-                           step/clip, as a param without grad is (adamw.cpp:89-90,133-134) */
+                           step/clip, as a param without grad is (adamw.cpp:30-31,74-75) */
     uint64_t numel;
     float weight_decay; /* this tensor's decoupled weight decay (per-param-group mask) */
 } soar_tensor_desc;
@@ -113,7 +113,7 @@ typedef struct soar_step_info {
 /* Reference-default options (adamw.hpp:10-16) and the extension defaults. */
 SOAR_API void soar_adamw_default_opts(soar_adamw_opts* out);
 
-/* Replaces AdamW::AdamW(std::vector<TensorPtr>, AdamWOptions) (adamw.cpp:66-77):
+/* Replaces AdamW::AdamW(std::vector<TensorPtr>, AdamWOptions) (adamw.cpp:7-18):
    allocates the optimizer state (m = v = 0; master = float(param) in the mixed
    layout) and the tensor-list chunk table on opts->device. */
 SOAR_API int soar_optim_create(const soar_tensor_desc* tensors, int n_tensors,
@@ -135,7 +135,7 @@ typedef struct soar_sgd_opts {
     float lr;               /* 1e-2 */
     float momentum;         /* 0 */
     float dampening;        /* 0 */
-    float weight_decay;     /* 0 (coupled: d_p += wd * theta, sgd.cpp:71-73) */
+    float weight_decay;     /* 0 (coupled: d_p += wd * theta, sgd.cpp:72-74) */
     int32_t nesterov;       /* 0 */
     int32_t layout;
     float max_grad_norm;
@@ -148,15 +148,15 @@ typedef struct soar_sgd_opts {
 } soar_sgd_opts;
 
 SOAR_API void soar_sgd_default_opts(soar_sgd_opts* out);
-/* Replaces SGD::SGD(std::vector<TensorPtr>, SGDOptions) (sgd.cpp:6-16). Each
+/* Replaces SGD::SGD(std::vector<TensorPtr>, SGDOptions) (sgd.cpp:7-16). Each
    tensor's weight_decay is its own (parameter groups). */
 SOAR_API int soar_sgd_create(const soar_tensor_desc* tensors, int n_tensors,
                              const soar_sgd_opts* opts, void** out_handle);
 
 SOAR_API int soar_optim_destroy(void* handle);
 
-/* Replaces AdamW::step() (adamw.cpp:119-176) -- and, with max_grad_norm > 0,
-   the clip_grad_norm() call before it (adamw.cpp:87-117) -- as one fused
+/* Replaces AdamW::step() (adamw.cpp:60-117) -- and, with max_grad_norm > 0,
+   the clip_grad_norm() call before it (adamw.cpp:28-58) -- as one fused
    device step: unscale, inf/NaN detect, global norm, clip, AdamW with
    per-tensor wd on the fp32 master, bf16 write-back, loss-scale update.
    Enqueued on `stream`; never synchronises the host. It may be captured into
@@ -169,7 +169,7 @@ SOAR_API int soar_optim_destroy(void* handle);
    capture-safe.) */
 SOAR_API int soar_optim_step(void* handle, void* stream);
 
-/* Replaces AdamW::clip_grad_norm(max_norm) (adamw.cpp:87-117): returns the
+/* Replaces AdamW::clip_grad_norm(max_norm) (adamw.cpp:28-58): returns the
    pre-clip global L2 norm in *out_norm and, when norm > max_norm and
    norm > 1e-6, scales the fp32 grads in place by max_norm/norm. In the mixed
    layout the bf16 grads are left untouched and the coefficient is applied in
@@ -178,7 +178,7 @@ SOAR_API int soar_optim_step(void* handle, void* stream);
 SOAR_API int soar_optim_clip_grad_norm(void* handle, float max_norm, float* out_norm,
                                        void* stream);
 
-/* Replaces AdamW::zero_grad() (adamw.cpp:79-85): zeroes every gradient. */
+/* Replaces AdamW::zero_grad() (adamw.cpp:20-26): zeroes every gradient. */
 SOAR_API int soar_optim_zero_grad(void* handle, void* stream);
 
 /* Replace AdamW::set_lr / get_lr (adamw.hpp:29-30). Host-side, no device work. */
@@ -223,7 +223,7 @@ SOAR_API int soar_optim_load_state(void* handle, const char* path, void* stream)
 
 /* Weight EMA fused into the update: replaces soar::utils::ModelEMA
    (include/soar/utils/ema.hpp:10-66). enable allocates the shadow and copies
-   the current fp32 weights into it (init_shadow, ema.hpp:52-58); from then on
+   the current fp32 weights into it (init_shadow, ema.hpp:49-57); from then on
    every applied step also computes shadow = decay*shadow + (1-decay)*weight
    (update, ema.hpp:18-28) inside the update kernel, on the fp32 master
    weights (the fp32 params in the FP32 layout), for +8 bytes per param.
@@ -317,27 +317,12 @@ SOAR_API int soar_zero1_set_signals(void* zero1_handle, void* const* signal_base
    checkpoint. */
 SOAR_API int soar_zero1_step(void* zero1_handle, void* stream);
 
-/* Measurement, no reference counterpart: the raw NVLink rate of the fused
-   step's two peer-memory access patterns, with no arithmetic, on symmetric
-   buffers of at least world * bytes_per_peer bytes (bases[q]: rank q's, as
-   seen from this process; 16-byte aligned). Every rank calls it at once.
-   mode 0 (pull, k_rs_sumsq's reads): bulk-loads bytes [rank * bytes_per_peer,
-   (rank + 1) * bytes_per_peer) of every peer's buffer into a shared-memory
-   ring of `stages` stages of tile_bytes per peer (stages * tile_bytes *
-   (world - 1) <= 200 KB). mode 1 (push, k_apply's all-gather writes):
-   bulk-stores zero tiles into that range of every peer's buffer (overwrites
-   it). tile_bytes: a multiple of 16 dividing bytes_per_peer. `grid` CTAs.
-   A wait that runs out (1 s) sets *d_err. */
-SOAR_API int soar_nvlink_probe(void* const* bases, int world, int rank, uint64_t bytes_per_peer,
-                               int mode, uint32_t tile_bytes, int stages, int grid, int* d_err,
-                               void* stream);
-
 /* Nonzero in *out_error if a device-side wait of the data-parallel step timed
    out (synchronises the device). */
 SOAR_API int soar_zero1_error(void* zero1_handle, int* out_error);
 SOAR_API int soar_zero1_destroy(void* zero1_handle);
 
-/* Replaces CosineAnnealingLR (adamw.hpp:45-57, adamw.cpp:178-202): linear
+/* Replaces CosineAnnealingLR (adamw.hpp:45-57, adamw.cpp:119-143): linear
    warmup, cosine decay to eta_min, eta_min past the end; each step() sets the
    bound optimizer's lr (host-side float math, the reference's expressions).
    The scheduler keeps the optimizer handle, so moving the optimizer between
@@ -360,7 +345,10 @@ SOAR_API int soar_cosine_destroy(void* sched_handle);
    At most SOAR_NOALLOC_MAX_TENSORS tensors per call (more is rejected with an
    error); element counts are unlimited. Runs on the current device. The first
    call on a device also sets up that device (looks up the array's device
-   address); make that first call before any stream capture. All calls share
+   address, cached for the life of the process: it assumes the device's
+   primary context lives as long, so a process that calls cudaDeviceReset must
+   not call this entry point afterwards); make that first call before any
+   stream capture. All calls share
    the array: calls whose kernels overlap on the GPU race and give wrong sums,
    so order them on one stream. */
 #define SOAR_NOALLOC_MAX_TENSORS 64
@@ -375,6 +363,13 @@ SOAR_API int soar_grad_sumsq_noalloc(const void* const* grads, const uint64_t* n
    No fault, trap or hang is involved; the context stays usable. */
 SOAR_API int soar_selftest_bounded_wait(uint64_t limit_ns, int device, int* out_timed_out,
                                         uint64_t* out_waited_ns);
+
+/* Build query, no reference counterpart. *out_compiled: the architecture the
+   kernels were compiled for, as nvcc's __CUDA_ARCH_LIST__ writes it (1000 for
+   sm_100a); needs no GPU. With device >= 0 also *out_loaded: the SASS version
+   the update kernel was loaded as on that device (cudaFuncGetAttributes
+   binaryVersion: 100 for sm_100a), which needs the GPU. */
+SOAR_API int soar_kernel_arch(int device, int* out_compiled, int* out_loaded);
 
 /* Message of the calling thread's last failed call ("" if none). */
 SOAR_API const char* soar_last_error(void);

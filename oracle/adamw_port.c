@@ -57,7 +57,7 @@ void oracle_bf16_to_f32_array(const uint16_t* in, float* out, size_t n) {
 
 /* ---- AdamW (reference src/optim/adamw.cpp) ------------------------------ */
 
-/* adamw.cpp:127-130: bias corrections for step t (t already incremented). */
+/* adamw.cpp:68-71: bias corrections for step t (t already incremented). */
 void oracle_adamw_coeffs(float lr, float beta1, float beta2, uint64_t t,
                          float* step_size, float* sqrt_bc2) {
     float bias_correction1 = 1.0f - powf(beta1, (float)t);
@@ -66,7 +66,7 @@ void oracle_adamw_coeffs(float lr, float beta1, float beta2, uint64_t t,
     *step_size = lr / bias_correction1;
 }
 
-/* adamw.cpp:149-167: the per-element update of one tensor, in place. */
+/* adamw.cpp:90-108: the per-element update of one tensor, in place. */
 void oracle_adamw_update_f32(float* theta, const float* g, float* m, float* v, size_t n,
                              float lr, float beta1, float beta2, float eps, float wd,
                              float step_size, float sqrt_bc2) {
@@ -82,17 +82,17 @@ void oracle_adamw_update_f32(float* theta, const float* g, float* m, float* v, s
     }
 }
 
-/* adamw.cpp:88-99: running double sum of squares, serial, in tensor order.
+/* adamw.cpp:29-40: running double sum of squares, serial, in tensor order.
  * Returns acc + sum_i g[i]^2. */
 double oracle_sumsq_f32(const float* g, size_t n, double acc) {
     for (size_t i = 0; i < n; ++i) acc += (double)g[i] * (double)g[i];
     return acc;
 }
 
-/* adamw.cpp:101 */
+/* adamw.cpp:42 */
 float oracle_norm_from_sumsq(double total_norm_sq) { return (float)sqrt(total_norm_sq); }
 
-/* adamw.cpp:102-103: returns the clip coefficient, or 1 (no clip). */
+/* adamw.cpp:43-44: returns the clip coefficient, or 1 (no clip). */
 float oracle_clip_coef(float total_norm, float max_norm, int* clipped) {
     if (total_norm > max_norm && total_norm > 1e-6f) {
         *clipped = 1;
@@ -102,12 +102,12 @@ float oracle_clip_coef(float total_norm, float max_norm, int* clipped) {
     return 1.0f;
 }
 
-/* adamw.cpp:108-110 */
+/* adamw.cpp:49-51 */
 void oracle_scale_f32(float* g, size_t n, float coef) {
     for (size_t i = 0; i < n; ++i) g[i] *= coef;
 }
 
-/* CosineAnnealingLR::step, adamw.cpp:182-201. current_step is the value after
+/* CosineAnnealingLR::step, adamw.cpp:123-142. current_step is the value after
  * the increment; base_lr is the optimizer lr at scheduler construction. */
 float oracle_cosine_lr(float base_lr, float eta_min, uint64_t total_steps,
                        uint64_t warmup_steps, uint64_t current_step) {
@@ -175,7 +175,7 @@ void oracle_scaler_update(oracle_step_state* st, int found_inf, float growth_fac
 }
 
 /* Sum of squares of the unscaled gradients of a tensor list, serial in tensor
- * order (adamw.cpp:88-99 on the unscaled grads). *found_inf is set when any
+ * order (adamw.cpp:29-40 on the unscaled grads). *found_inf is set when any
  * unscaled value is non-finite. scratch must hold max(numel) floats. */
 double oracle_grad_sumsq(int layout, int n_tensors, void** grads, const uint64_t* numel,
                          float inv_scale, int* found_inf, float* scratch) {
@@ -245,7 +245,7 @@ int oracle_apply_with_sumsq(int layout, int n_tensors, void** params, void** gra
  *   bf16 params = RNE(master) in the mixed layout; scaler update.
  * layout 0: params/grads are fp32 (params are the master, updated in place).
  * layout 1: params/grads are bf16, master holds the fp32 weights.
- * Tensors with a NULL grad are skipped (adamw.cpp:89-90,133-134).
+ * Tensors with a NULL grad are skipped (adamw.cpp:30-31,74-75).
  * scratch must hold max(numel) floats. Returns 1 when the step was skipped.
  * (found_inf is carried by the sum itself: any non-finite unscaled value
  * makes the fp64 sum of squares non-finite.) */
@@ -263,10 +263,10 @@ int oracle_step(int layout, int n_tensors, void** params, void** grads, float** 
                                    backoff_factor, growth_interval, sumsq, st, scratch);
 }
 
-/* ---- SGD (reference src/optim/sgd.cpp:52-98) ---------------------------- */
+/* ---- SGD (reference src/optim/sgd.cpp:52-96) ---------------------------- */
 
-/* One tensor's SGD::step body (sgd.cpp:68-86); has_buf: the momentum buffer
- * holds a previous step (has_momentum_buffer_, sgd.cpp:89). */
+/* One tensor's SGD::step body (sgd.cpp:70-88); has_buf: the momentum buffer
+ * holds a previous step (has_momentum_buffer_, sgd.cpp:90). */
 void oracle_sgd_update_f32(float* theta, const float* grad, float* buf, size_t n, float lr,
                            float momentum, float dampening, float weight_decay, int nesterov,
                            int has_buf) {

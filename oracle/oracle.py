@@ -29,7 +29,26 @@ HERE = Path(__file__).resolve().parent
 PORT_SO = HERE / "liboracle_port.so"
 REF_SO = HERE / "_ref" / "libsoar_ref_adamw.so"
 REF_CUDA_SO = HERE / "_ref" / "libsoar_ref_cuda.so"
-REF_ROOT = Path(os.environ.get("SOAR_REF_ROOT", "/root/reference"))
+
+
+def _ref_root() -> Path | None:
+    """Root of the reference source tree: $SOAR_REF_ROOT, else the
+    `reference_path` recorded in the repository's BASELINE.json. None when
+    neither names an existing tree (the compiled oracle then comes from an
+    earlier build, or is absent)."""
+    cand = os.environ.get("SOAR_REF_ROOT")
+    if not cand:
+        try:
+            import json
+            cand = json.loads((HERE.parent / "BASELINE.json").read_text()).get("reference_path")
+        except (OSError, ValueError):
+            cand = None
+    if cand and (Path(cand) / "src" / "optim" / "adamw.cpp").exists():
+        return Path(cand)
+    return None
+
+
+REF_ROOT = _ref_root()
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
@@ -39,8 +58,10 @@ def build(ref: bool | None = None) -> None:
     """Compile the port (always) and the reference oracle (when its sources exist)."""
     subprocess.run(["make", "-s", "-C", str(HERE), "port"], check=True)
     if ref is None:
-        ref = (REF_ROOT / "src" / "optim" / "adamw.cpp").exists()
+        ref = REF_ROOT is not None
     if ref:
+        if REF_ROOT is None:
+            raise FileNotFoundError("reference sources not found: set SOAR_REF_ROOT")
         subprocess.run(["make", "-s", "-C", str(HERE), "ref", "refcuda", f"REF_ROOT={REF_ROOT}"],
                        check=True)
 
@@ -216,7 +237,7 @@ class PortOptimizer:
         return self.master[i] if self.cfg.layout == 1 else self.params[i]
 
     def enable_ema(self, decay: float):
-        """ModelEMA: the shadow starts as a copy of the weights (ema.hpp:52-58)."""
+        """ModelEMA: the shadow starts as a copy of the weights (ema.hpp:49-57)."""
         self.ema = [self.weights(i).astype(np.float32).copy() for i in range(len(self.params))]
         self.ema_decay = decay
 
@@ -507,7 +528,7 @@ class RefComposite:
             self.master = [bf16_to_f32(p) for p in self.params]
         else:
             self.master = self.params
-        # tensors without a gradient are skipped by the reference (adamw.cpp:89-90,133-134)
+        # tensors without a gradient are skipped by the reference (adamw.cpp:30-31,74-75)
         self.gbuf = [None if i in null_grad else np.zeros(p.size, np.float32)
                      for i, p in enumerate(self.params)]
         self.wd = [float(np.float32(w)) for w in wd]

@@ -53,7 +53,7 @@ struct RefSched {
 extern "C" {
 
 // params[i]/grads[i]: host fp32 buffers of numel[i] elements. grads[i] may be
-// NULL: the reference then skips that param (adamw.cpp:89-90,133-134).
+// NULL: the reference then skips that param (adamw.cpp:30-31,74-75).
 void* soar_ref_adamw_create(float** params, float** grads, const uint64_t* numel, int n,
                             float lr, float beta1, float beta2, float eps, float wd) {
     auto* h = new RefOptim();

@@ -137,7 +137,10 @@ k_grad_sumsq_noalloc(TensorList tl, Scratch* __restrict__ scratch, double* __res
 
 // Per-device set-up, done once by the first call on each device: the device
 // address of g_noalloc_scratch (in host code the symbol's name only stands in
-// for it) and the launch width.
+// for it) and the launch width. The address is cached for the life of the
+// process, so it assumes the device's primary context lives as long: after a
+// cudaDeviceReset the cached address no longer belongs to the new context, and
+// this entry point must not be called again in that process.
 struct DeviceSetup {
     Scratch* scratch = nullptr;
     int grid = 0;

@@ -12,19 +12,24 @@
 //
 // All ranks run it at once, so each GPU's links carry both directions, as in
 // the step. Every wait is bounded (1 s) and reported through `err`.
+//
+// A measurement tool, not part of the optimizer library: it builds into its
+// own library (libsoar_probe.so), declared in bench_probe.h, which only the
+// bench loads.
 #include <cstdint>
 #include <string>
 
 #include <cuda_runtime.h>
 
-#include "../../include/soar_optim.h"
+#include "bench_probe.h"
 #include "optim_kernels.cuh"
 #include "pipeline.cuh"
 
 namespace soarb {
-void record_error(const std::string& msg);  // optim_capi.cu
-
 namespace {
+
+thread_local std::string g_probe_error;
+void record_error(const std::string& msg) { g_probe_error = msg; }
 
 constexpr int kProbeMaxStages = 8;
 constexpr size_t kProbeMaxSmem = 200 * 1024;
@@ -86,25 +91,29 @@ __global__ void k_probe_push(ProbePeers peers, int world, int rank, uint64_t byt
 }  // namespace
 }  // namespace soarb
 
-extern "C" SOAR_API int soar_nvlink_probe(void* const* bases, int world, int rank,
+extern "C" SOAR_PROBE_API const char* soar_probe_last_error(void) {
+    return soarb::g_probe_error.c_str();
+}
+
+extern "C" SOAR_PROBE_API int soar_nvlink_probe(void* const* bases, int world, int rank,
                                           uint64_t bytes_per_peer, int mode, uint32_t tile_bytes,
                                           int stages, int grid, int* d_err, void* stream) {
     using namespace soarb;
     if (!bases || !d_err || world < 2 || world > kMaxRanks || rank < 0 || rank >= world ||
         grid < 1 || (mode != 0 && mode != 1)) {
         record_error("soar_nvlink_probe: bad argument");
-        return SOAR_ERROR;
+        return -1;
     }
     if (tile_bytes == 0 || tile_bytes % 16 || bytes_per_peer % tile_bytes) {
         record_error("soar_nvlink_probe: tile_bytes must be a nonzero multiple of 16 dividing "
                      "bytes_per_peer");
-        return SOAR_ERROR;
+        return -1;
     }
     ProbePeers p{};
     for (int r = 0; r < world; ++r) {
         if (!bases[r] || reinterpret_cast<uintptr_t>(bases[r]) % 16) {
             record_error("soar_nvlink_probe: null or unaligned buffer");
-            return SOAR_ERROR;
+            return -1;
         }
         p.base[r] = static_cast<char*>(bases[r]);
     }
@@ -114,7 +123,7 @@ extern "C" SOAR_API int soar_nvlink_probe(void* const* bases, int world, int ran
         const size_t smem = static_cast<size_t>(stages) * tile_bytes * (world - 1);
         if (stages < 1 || stages > kProbeMaxStages || smem > kProbeMaxSmem) {
             record_error("soar_nvlink_probe: stages x tile x (world - 1) exceeds the ring");
-            return SOAR_ERROR;
+            return -1;
         }
         e = cudaFuncSetAttribute(k_probe_pull, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(smem));
@@ -126,7 +135,7 @@ extern "C" SOAR_API int soar_nvlink_probe(void* const* bases, int world, int ran
     } else {
         if (tile_bytes > kProbeMaxSmem) {
             record_error("soar_nvlink_probe: tile exceeds shared memory");
-            return SOAR_ERROR;
+            return -1;
         }
         e = cudaFuncSetAttribute(k_probe_push, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  static_cast<int>(tile_bytes));
@@ -137,7 +146,7 @@ extern "C" SOAR_API int soar_nvlink_probe(void* const* bases, int world, int ran
     }
     if (e != cudaSuccess) {
         record_error(std::string("soar_nvlink_probe: ") + cudaGetErrorString(e));
-        return SOAR_ERROR;
+        return -1;
     }
-    return SOAR_OK;
+    return 0;
 }

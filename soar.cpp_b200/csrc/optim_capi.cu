@@ -119,7 +119,7 @@ struct Cosine {
 size_t elem_bytes(const Optim& o) { return o.mixed ? 2 : 4; }
 
 // bc[t] = (1 - beta1^t, sqrt(1 - beta2^t)) with the reference's own host
-// expressions (adamw.cpp:127-129), so the device reads the reference's bits.
+// expressions (adamw.cpp:68-70), so the device reads the reference's bits.
 std::vector<float2> bias_table(float beta1, float beta2, uint32_t len, bool* converged) {
     std::vector<float2> tab(len);
     tab[0] = make_float2(1.0f, 1.0f);  // t = 0 is never used
@@ -517,7 +517,7 @@ soarb::ApplyArgs apply_args(const Optim& o, const double* parts, int n_parts) {
     a.beta1 = o.opts.beta1;
     a.beta2 = o.opts.beta2;
     a.eps = o.opts.eps;
-    // adamw.cpp:159-160 evaluate (1.0f - beta) in float on the host
+    // adamw.cpp:100-101 evaluate (1.0f - beta) in float on the host
     a.omb1 = 1.0f - o.opts.beta1;
     a.omb2 = 1.0f - o.opts.beta2;
     a.max_norm = o.opts.max_grad_norm;
@@ -532,12 +532,12 @@ soarb::ApplyArgs apply_args(const Optim& o, const double* parts, int n_parts) {
     a.bc_len = o.bc_len;
     if (o.sgd) {
         a.momentum = o.momentum;
-        a.omdamp = 1.0f - o.dampening;  // sgd.cpp:80 evaluates (1.0f - dampening) in float
+        a.omdamp = 1.0f - o.dampening;  // sgd.cpp:79 evaluates (1.0f - dampening) in float
         a.nesterov = o.nesterov ? 1 : 0;
     }
     if (o.ema) {
         a.ema_decay = o.ema_decay;
-        a.ema_omd = 1.0f - o.ema_decay;  // ema.hpp:24 evaluates (1.0f - decay_) in float
+        a.ema_omd = 1.0f - o.ema_decay;  // ema.hpp:25 evaluates (1.0f - decay_) in float
         a.ema_delta = static_cast<long long>(o.ema - o.m);
     }
     return a;
@@ -748,7 +748,7 @@ SOAR_API int soar_optim_clip_grad_norm(void* handle, float max_norm, float* out_
     double total = 0.0;
     SOAR_CUDA_TRY(cudaMemcpyAsync(&total, o.sumsq_scratch, sizeof total, cudaMemcpyDeviceToHost, s));
     SOAR_CUDA_TRY(cudaStreamSynchronize(s));
-    // adamw.cpp:101-103
+    // adamw.cpp:42-44
     const float total_norm = static_cast<float>(std::sqrt(total));
     if (total_norm > max_norm && total_norm > 1e-6f) {
         const float clip_coef = max_norm / total_norm;
@@ -905,7 +905,7 @@ SOAR_API int soar_optim_enable_ema(void* handle, float decay, void* stream) {
         o.ema = e;
     }
     o.ema_decay = decay;
-    // ModelEMA::init_shadow (ema.hpp:52-58): the shadow starts as a copy of the weights
+    // ModelEMA::init_shadow (ema.hpp:49-57): the shadow starts as a copy of the weights
     for (const TensorRec& t : o.tensors) {
         if (!t.numel) continue;
         const float* w = o.mixed ? o.master + t.state_off : static_cast<const float*>(t.param);
@@ -1095,7 +1095,7 @@ SOAR_API int soar_cosine_create(void* optim_handle, uint64_t total_steps, float 
                                 uint64_t warmup_steps, void** out_handle) {
     if (!optim_handle || !out_handle) return fail("null argument");
     Optim* o = as_optim(optim_handle);
-    // adamw.cpp:178-180: base lr is the optimizer's lr at construction
+    // adamw.cpp:119-121: base lr is the optimizer's lr at construction
     *out_handle = new (std::nothrow) Cosine{o, o->lr, eta_min, total_steps, warmup_steps, 0};
     return *out_handle ? SOAR_OK : fail("out of host memory");
 }
@@ -1103,7 +1103,7 @@ SOAR_API int soar_cosine_create(void* optim_handle, uint64_t total_steps, float 
 SOAR_API int soar_cosine_step(void* sched_handle) {
     if (!sched_handle) return fail("null handle");
     Cosine& c = *static_cast<Cosine*>(sched_handle);
-    // adamw.cpp:182-201, same types and expressions
+    // adamw.cpp:123-142, same types and expressions
     c.current_step++;
     if (c.current_step <= c.warmup_steps && c.warmup_steps > 0) {
         const float lr = c.base_lr * static_cast<float>(c.current_step) /
@@ -1148,6 +1148,21 @@ SOAR_API int soar_selftest_bounded_wait(uint64_t limit_ns, int device, int* out_
     if (e != cudaSuccess) return fail(std::string("selftest: ") + cudaGetErrorString(e));
     *out_timed_out = err;
     *out_waited_ns = ns;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_kernel_arch(int device, int* out_compiled, int* out_loaded) {
+    if (!out_compiled) return fail("null argument");
+    // the architectures nvcc compiled the kernels for (first entry), e.g. 1000
+    constexpr int kArchs[] = {__CUDA_ARCH_LIST__};
+    *out_compiled = kArchs[0];
+    if (device < 0) return SOAR_OK;
+    if (!out_loaded) return fail("null argument");
+    DeviceGuard g(device);
+    if (!g.ok) return fail("cannot select device " + std::to_string(device));
+    cudaFuncAttributes attr{};
+    SOAR_CUDA_TRY(soarb::apply_kernel_attributes(&attr));
+    *out_loaded = attr.binaryVersion;
     return SOAR_OK;
 }
 

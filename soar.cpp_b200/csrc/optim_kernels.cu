@@ -28,7 +28,7 @@
 //                 finish commits the step counters and the loss-scaler update.
 //
 // Numerics follow the reference's AdamW::step / clip_grad_norm
-// (src/optim/adamw.cpp:87-176) operation for operation with explicitly
+// (src/optim/adamw.cpp:28-117) operation for operation with explicitly
 // rounded intrinsics (no contraction, IEEE sqrt and division), so the fp32
 // update reproduces the reference's bits.
 //
@@ -68,7 +68,7 @@ __device__ __forceinline__ double block_sum(double x, double* smem /* >= 32 */) 
 
 // Sum of (double(g * inv))^2. The square of a float is exact in double, so an
 // fma here equals the reference's separate multiply and add
-// (adamw.cpp:96-97) term by term; only the summation order differs.
+// (adamw.cpp:37-38) term by term; only the summation order differs.
 __device__ __forceinline__ double sq_acc(double acc, float g) {
     const double d = static_cast<double>(g);
     return fma(d, d, acc);
@@ -169,10 +169,10 @@ struct StepCoeffs {
     float coef;       // clip coefficient (1: no clip)
     float step_size;  // lr / bias_correction1 (AdamW)
     float sqrt_bc2;   // (AdamW)
-    int has_buf;      // SGD: momentum buffers hold a previous step (sgd.cpp:74-80)
+    int has_buf;      // SGD: momentum buffers hold a previous step (sgd.cpp:75-80)
 };
 
-// One element of SGD::step (reference src/optim/sgd.cpp:68-86): coupled weight
+// One element of SGD::step (reference src/optim/sgd.cpp:70-88): coupled weight
 // decay, momentum with dampening, optional Nesterov, theta -= lr * d_p. `m`
 // is the momentum buffer.
 __device__ __forceinline__ void sgd_elem(float& th, float& m, float g, const ApplyArgs& a,
@@ -186,7 +186,7 @@ __device__ __forceinline__ void sgd_elem(float& th, float& m, float g, const App
     th = __fsub_rn(th, __fmul_rn(a.lr, d));
 }
 
-// One element of AdamW::step (adamw.cpp:151-166) on an unscaled, clipped grad.
+// One element of AdamW::step (adamw.cpp:92-107) on an unscaled, clipped grad.
 __device__ __forceinline__ void adamw_elem(float& th, float& m, float& v, float g,
                                            const ApplyArgs& a, const StepCoeffs& k, float lr_wd,
                                            bool has_wd) {
@@ -197,12 +197,12 @@ __device__ __forceinline__ void adamw_elem(float& th, float& m, float& v, float 
     th = __fsub_rn(th, __fmul_rn(k.step_size, __fdiv_rn(m, denom)));
 }
 
-// Unscale (exact for power-of-two scales) then clip (adamw.cpp:108-110).
+// Unscale (exact for power-of-two scales) then clip (adamw.cpp:49-51).
 __device__ __forceinline__ float prep_grad(float graw, const StepCoeffs& k) {
     return __fmul_rn(__fmul_rn(graw, k.inv), k.coef);
 }
 
-// ModelEMA::update (ema.hpp:24) for one weight: decay*shadow + (1-decay)*weight.
+// ModelEMA::update (ema.hpp:25) for one weight: decay*shadow + (1-decay)*weight.
 __device__ __forceinline__ float ema_elem(float sh, float w, const ApplyArgs& a) {
     return __fadd_rn(__fmul_rn(a.ema_decay, sh), __fmul_rn(a.ema_omd, w));
 }
@@ -311,9 +311,9 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
             double s = 0.0;
             for (int p = 0; p < a.n_parts; ++p) s += a.parts[p];
             found = !isfinite(s);
-            norm = __double2float_rn(__dsqrt_rn(s));  // adamw.cpp:101
+            norm = __double2float_rn(__dsqrt_rn(s));  // adamw.cpp:42
             if (a.use_scaler && found) skip = 1;
-            // adamw.cpp:102-103: no eps, no min(1, .)
+            // adamw.cpp:43-44: no eps, no min(1, .)
             if (a.max_norm > 0.0f && norm > a.max_norm && norm > 1e-6f)
                 coef = __fdiv_rn(a.max_norm, norm);
         }
@@ -323,7 +323,7 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
         StepCoeffs k;
         k.inv = a.use_scaler ? __fdiv_rn(1.0f, ctl->scale) : 1.0f;
         k.coef = coef;
-        k.step_size = __fdiv_rn(a.lr, bc.x);  // adamw.cpp:130
+        k.step_size = __fdiv_rn(a.lr, bc.x);  // adamw.cpp:71
         k.sqrt_bc2 = bc.y;
         k.has_buf = ctl->t > 0;  // applied steps so far (skipped steps never fill buffers)
         s_k = k;
@@ -589,7 +589,7 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
 
 // ------------------------------------------------------------ small kernels --
 
-// In-place fp32 clip of the gradients (adamw.cpp:104-110).
+// In-place fp32 clip of the gradients (adamw.cpp:45-51).
 __global__ void __launch_bounds__(kThreads)
 k_scale_grads_f32(const Chunk* __restrict__ chunks, int n_chunks, float coef) {
     for (int c = blockIdx.x; c < n_chunks; c += gridDim.x) {
@@ -771,6 +771,10 @@ cudaError_t launch_wait_selftest(uint64_t limit_ns, int* out_error, unsigned lon
                                  cudaStream_t stream) {
     k_wait_selftest<<<1, 32, 0, stream>>>(limit_ns, out_error, out_ns);
     return cudaGetLastError();
+}
+
+cudaError_t apply_kernel_attributes(cudaFuncAttributes* out) {
+    return cudaFuncGetAttributes(out, k_apply<true, false, false, false, false>);
 }
 
 int occupancy_grad_sumsq(bool bf16) {

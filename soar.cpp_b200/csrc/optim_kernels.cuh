@@ -178,6 +178,10 @@ cudaError_t launch_step_done(Signals* const* sig, int world, int rank, uint64_t 
 cudaError_t launch_wait_selftest(uint64_t limit_ns, int* out_error, unsigned long long* out_ns,
                                  cudaStream_t stream);
 
+// Attributes of the loaded update kernel (binaryVersion: the SASS target it
+// was loaded as, 100 for sm_100a).
+cudaError_t apply_kernel_attributes(cudaFuncAttributes* out);
+
 // One-time per-process kernel attribute set-up (dynamic shared memory size).
 cudaError_t prepare_kernels();
 

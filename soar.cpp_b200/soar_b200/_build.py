@@ -14,8 +14,12 @@ LIBDIR = ROOT / "lib"
 LIB = LIBDIR / "libsoar_optim.so"
 INCLUDE = ROOT.parent / "include"
 
-SOURCES = ["optim_kernels.cu", "optim_capi.cu", "noalloc_sumsq.cu", "zero1.cu", "nvlink_probe.cu"]
+SOURCES = ["optim_kernels.cu", "optim_capi.cu", "noalloc_sumsq.cu", "zero1.cu"]
 HEADERS = ["optim_kernels.cuh", "pipeline.cuh"]
+# the bench-only NVLink probe: a library of its own, not part of the C-ABI
+PROBE_LIB = LIBDIR / "libsoar_probe.so"
+PROBE_SOURCES = ["nvlink_probe.cu"]
+PROBE_HEADERS = ["bench_probe.h", "optim_kernels.cuh", "pipeline.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -72,3 +76,19 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     subprocess.run(cmd, check=True)
     tmp.replace(LIB)
     return LIB
+
+
+def build_probe(force: bool = False, verbose: bool = False) -> Path:
+    """The bench-only NVLink probe library (csrc/bench_probe.h)."""
+    deps = [CSRC / s for s in PROBE_SOURCES + PROBE_HEADERS]
+    if not force and PROBE_LIB.exists() and \
+            all(d.stat().st_mtime <= PROBE_LIB.stat().st_mtime for d in deps):
+        return PROBE_LIB
+    LIBDIR.mkdir(exist_ok=True)
+    tmp = PROBE_LIB.with_suffix(f".so.tmp{os.getpid()}")
+    cmd = [nvcc(), *NVCC_FLAGS, "-o", str(tmp), *[str(CSRC / s) for s in PROBE_SOURCES]]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True)
+    tmp.replace(PROBE_LIB)
+    return PROBE_LIB

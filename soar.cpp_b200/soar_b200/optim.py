@@ -116,11 +116,10 @@ SIGNATURES: dict[str, tuple] = {
     "soar_zero1_set_signals": (C.c_int, [C.c_void_p, C.c_void_p]),
     "soar_zero1_step": (C.c_int, [C.c_void_p, C.c_void_p]),
     "soar_zero1_error": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
-    "soar_nvlink_probe": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_uint64, C.c_int,
-                                    C.c_uint32, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
     "soar_zero1_destroy": (C.c_int, [C.c_void_p]),
     "soar_selftest_bounded_wait": (C.c_int, [C.c_uint64, C.c_int, C.POINTER(C.c_int),
                                              C.POINTER(C.c_uint64)]),
+    "soar_kernel_arch": (C.c_int, [C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "soar_last_error": (C.c_char_p, []),
 }
 
@@ -134,6 +133,23 @@ class Zero1Shard(C.Structure):
 
 def library_path() -> Path:
     return _build.LIB
+
+
+_probe: C.CDLL | None = None
+
+
+def probe_lib() -> C.CDLL:
+    """The bench-only NVLink probe library (bench_probe.h), built on first use."""
+    global _probe
+    if _probe is None:
+        handle = C.CDLL(str(_build.build_probe()))
+        handle.soar_nvlink_probe.restype = C.c_int
+        handle.soar_nvlink_probe.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_uint64, C.c_int,
+                                             C.c_uint32, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
+        handle.soar_probe_last_error.restype = C.c_char_p
+        handle.soar_probe_last_error.argtypes = []
+        _probe = handle
+    return _probe
 
 
 def lib() -> C.CDLL:

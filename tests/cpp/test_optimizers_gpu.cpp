@@ -116,7 +116,7 @@ void test_trainer_sequence_and_move() {
     // moved into its owner (trainer.hpp:100), with the scheduler bound first
     // (main.cpp:712-716): the scheduler must still drive the moved optimizer.
     auto p = make({1.0f, -2.0f, 0.5f});
-    auto p2 = make({0.25f});  // no grad: skipped (adamw.cpp:133-134)
+    auto p2 = make({0.25f});  // no grad: skipped (adamw.cpp:74-75)
     p->set_grad(make({0.1f, 0.2f, -0.3f}));
     soar::optim::AdamWOptions o;
     o.lr = 1e-2f;

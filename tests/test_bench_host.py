@@ -79,3 +79,52 @@ def test_cpu_sample_child_runs_on_one_thread():
     assert r.returncode == 0, r.stderr[-2000:]
     d = json.loads([x for x in r.stdout.splitlines() if x.startswith("{")][-1])
     assert d["cores"] == 1 and d["value"] > 0
+
+
+def test_reference_arm_uses_every_host_thread_under_torchrun_settings():
+    """torchrun sets OMP_NUM_THREADS=1; the reference arm still times the
+    reference on every host CPU (the child gets its own OMP_NUM_THREADS), on
+    the config's own workload, and the line says so."""
+    env = dict(os.environ, OMP_NUM_THREADS="1", RANK="0", WORLD_SIZE="2")
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference",
+                        "--params", "300000", "--steps", "2", "--warmup", "1", "--gpus", "2"],
+                       env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    d = json.loads([x for x in r.stdout.splitlines() if x.startswith("{")][-1])
+    assert d["impl"] == "reference" and d["config"]["same_config"] is True
+    assert d["cpu_baseline"]["cores"] == bench.host_threads() == d["config"]["threads"]
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["value"] == d["e2e"]["value"]
+
+
+def test_reference_arm_other_ranks_exit_without_work():
+    env = dict(os.environ, RANK="3", WORLD_SIZE="4")
+    r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference"],
+                       env=env, capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and not r.stdout.strip()
+
+
+def test_reference_sample_loads_nothing_of_the_package():
+    """The reference's timing process maps only oracle libraries: no library
+    of this package (the input generator included)."""
+    code = ("import sys; sys.path.insert(0, %r); import bench; "
+            "bench.cpu_reference_sample(100000, 1); "
+            "print('\\n'.join(l for l in open('/proc/self/maps').read().splitlines() "
+            "if '.so' in l))" % str(ROOT))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr[-2000:]
+    ours = [l for l in r.stdout.splitlines() if str(ROOT) in l]
+    assert ours and all("/oracle/" in l for l in ours), ours
+    assert "soar_b200" not in r.stdout and "soar.cpp_b200" not in r.stdout
+
+
+def test_nvlink_roofline_is_recomputable_from_the_phases():
+    phases = {"barrier": 0.01, "reduce_scatter+sumsq": 0.55, "partial_allgather": 0.02,
+              "update+allgather": 0.57, "barrier2": 0.01}
+    shard = 25_000_000
+    r = bench.nvlink_roofline(8, shard, phases, 1.2)
+    assert r["bound"] == "nvlink"
+    nbytes = 2 * 7 * shard * 2
+    assert r["bytes_per_step"] == nbytes
+    assert abs(r["achieved"] - nbytes / (1.12e-3) / 1e9) < 1e-6
+    assert abs(r["frac"] - r["achieved"] / bench.NVLINK_PEER_COPY_GBS) < 1e-12
+    assert abs(r["frac_spec"] - r["achieved"] / bench.NVLINK_SPEC_GBS) < 1e-12

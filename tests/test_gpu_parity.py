@@ -246,3 +246,13 @@ def test_async_info_matches_sync(cuda):
         assert info.grad_norm == want.grad_norm and info.clip_coef == want.clip_coef
         scale = want.loss_scale
     run.opt.close()
+
+
+def test_loaded_kernels_are_sm100a(cuda):
+    """The update kernel runs as sm_100a SASS on the device (binaryVersion 100),
+    and the library reports the architecture it was compiled for."""
+    import ctypes
+    compiled, loaded = ctypes.c_int(), ctypes.c_int()
+    assert sb.lib().soar_kernel_arch(0, ctypes.byref(compiled), ctypes.byref(loaded)) == 0
+    assert compiled.value == 1000
+    assert loaded.value == 100
