@@ -25,8 +25,8 @@ Rank 0 prints one JSON line. Besides the timed step it carries:
   parity    after the timed region, one more step checked against the CPU
             oracle on a sample of rank 0's shard, plus bit-identical params and
             counters on every rank;
-  configs   (N = 1) BASELINE configs 1-3 and config-5 sizes, each step timed
-            alone after an L2 flush.
+  configs   (N = 1) BASELINE configs 1-3 and config-5 sizes, cold-L2 steps
+            back to back over several copies, and one cold step alone.
 
 `--impl reference` times the reference's own CPU AdamW (oracle/_ref: the
 unmodified src/optim/adamw.cpp; the port oracle if that was not built) on the
@@ -89,7 +89,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--params", type=int, default=N_PARAMS)
-    ap.add_argument("--e2e-steps", type=int, default=6)
+    ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs", action="store_true",
                     help="leave the configs key out of the N=1 line")
@@ -470,10 +470,20 @@ def run_ours(args):
     # params (the ranks' shards together are the whole model once; at N = 1
     # the whole model)
     own = [(b.own_start, b.own_size) for b in z.buckets if b.own_size > 0]
+    grad_bufs, use_set = [grads], None
+    if world == 1:
+        # a second gradient buffer registered with the optimizer as gradient
+        # set 1: the upload of step s+1 lands there while step s reads set 0
+        grads2 = torch.empty_like(grads)
+        z.opt.add_grads([grads2[b.start:b.start + b.size] for b in z.buckets])
+        grad_bufs, use_set = [grads, grads2], z.opt.use_grads
     barrier()
     torch.cuda.synchronize()
-    e2e_ms = e2e_overlapped(torch, z.step, stream, grads, params, g_pin, p_pin, own,
-                            args.e2e_steps)
+    e2e_ms, e2e_copies = e2e_overlapped(torch, z.step, stream, grad_bufs, use_set, params,
+                                        g_pin, p_pin, own, args.e2e_steps)
+    if use_set is not None:
+        use_set(0)
+        del grad_bufs, grads2
     t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
     if comm:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -554,9 +564,12 @@ def run_ours(args):
         "e2e": {"value": world * n * args.e2e_steps / (e2e_ms * 1e-3) / 1e9, "unit": UNIT,
                 "h2d_bytes_per_step": 2 * n, "d2h_bytes_per_step": 2 * shard_params,
                 "transfers": "per rank: H2D of its full bf16 gradient from pinned memory, D2H "
-                             "of its updated shard of the bf16 params; read-back of step s "
-                             "overlaps the upload of step s+1 (two copy streams)",
-                "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps},
+                             "of its updated shard of the bf16 params (from a device snapshot); "
+                             "two copy streams, so the read-back of step s overlaps the upload "
+                             "of step s+1" + (", which lands in a second gradient set while "
+                                              "step s runs" if world == 1 else ""),
+                "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps,
+                "copies": e2e_copies},
         "clocks": clock_info,
         "gpu_launches": launches_per_step * args.steps,
         "phases_ms": phases,
@@ -573,39 +586,63 @@ def run_ours(args):
     return 0
 
 
-def e2e_overlapped(torch, step, stream, grads, params, g_pin, p_pin, own, steps) -> float:
+def e2e_overlapped(torch, step, stream, grad_bufs, use_set, params, g_pin, p_pin, own,
+                   steps) -> tuple[float, dict]:
     """`steps` steps through the public API with host buffers, timed on
-    `stream` with CUDA events. Step s: H2D of the gradient on one copy stream
-    once step s-1 has consumed the previous one; the step on `stream` once the
-    upload has landed and the read-back of step s-1 has left the parameter
-    buffer; D2H of the updated params on a second copy stream. Both PCIe
-    directions run at once (the read-back of step s beside the upload of step
-    s+1). Returns ms for all steps."""
+    `stream` with CUDA events. Step s uploads the gradient into buffer s mod B
+    (B = len(grad_bufs); with B = 2 the optimizer alternates between two
+    registered gradient sets, so the upload of step s+1 overlaps step s) on one
+    copy stream, once the step that last read that buffer is done; runs the
+    step on `stream`; copies the updated params into one of two device
+    snapshots (a device-to-device copy), which a second copy stream reads back
+    to the host. Both PCIe directions run at once and the step never waits
+    for a read-back. Returns (ms for all steps, copy timings)."""
+    nb = len(grad_bufs)
     h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
-    up = [torch.cuda.Event() for _ in range(steps)]
-    done = [torch.cuda.Event() for _ in range(steps)]
-    back = [torch.cuda.Event() for _ in range(steps)]
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    snaps = [torch.empty_like(params), torch.empty_like(params)]
+    ev = lambda timing=False: torch.cuda.Event(enable_timing=timing)
+    up, used, done, back = ([ev() for _ in range(steps)] for _ in range(4))
+    t_up = [(ev(True), ev(True)) for _ in range(steps)]
+    t_back = [(ev(True), ev(True)) for _ in range(steps)]
+    e0, e1 = ev(True), ev(True)
     e0.record(stream)
     for s in range(steps):
-        h2d.wait_event(done[s - 1] if s else e0)
+        b = s % nb
+        h2d.wait_event(used[s - nb] if s >= nb else e0)   # buffer b consumed by its last step
+        t_up[s][0].record(h2d)
         with torch.cuda.stream(h2d):
-            grads.copy_(g_pin, non_blocking=True)
+            grad_bufs[b].copy_(g_pin, non_blocking=True)
+        t_up[s][1].record(h2d)
         up[s].record(h2d)
         stream.wait_event(up[s])
-        if s:
-            stream.wait_event(back[s - 1])
+        if use_set is not None:
+            use_set(b)
         step()
+        used[s].record(stream)
+        if s >= 2:
+            stream.wait_event(back[s - 2])                # snapshot s % 2 read back
+        for lo, sz in own:
+            snaps[s % 2][lo:lo + sz].copy_(params[lo:lo + sz])
         done[s].record(stream)
         d2h.wait_event(done[s])
+        t_back[s][0].record(d2h)
         with torch.cuda.stream(d2h):
             for lo, sz in own:
-                p_pin[lo:lo + sz].copy_(params[lo:lo + sz], non_blocking=True)
+                p_pin[lo:lo + sz].copy_(snaps[s % 2][lo:lo + sz], non_blocking=True)
+        t_back[s][1].record(d2h)
         back[s].record(d2h)
     stream.wait_event(back[steps - 1])
     e1.record(stream)
     torch.cuda.synchronize()
-    return e0.elapsed_time(e1)
+    h2d_ms = statistics.mean(a.elapsed_time(b) for a, b in t_up)
+    d2h_ms = statistics.mean(a.elapsed_time(b) for a, b in t_back)
+    gb_up = g_pin.numel() * g_pin.element_size() / 1e9
+    gb_back = sum(sz for _, sz in own) * params.element_size() / 1e9
+    copies = {"h2d_ms": round(h2d_ms, 3), "d2h_ms": round(d2h_ms, 3),
+              "h2d_gbs": round(gb_up / (h2d_ms * 1e-3), 1),
+              "d2h_gbs": round(gb_back / (d2h_ms * 1e-3), 1), "grad_buffers": nb}
+    del snaps
+    return e0.elapsed_time(e1), copies
 
 
 def parity_check(torch, np, z, world, rank, comm, g_pin, grads, params) -> dict:
@@ -908,60 +945,93 @@ def config_specs(sizes5=(1_000_000, 16_000_000, 256_000_000)):
 
 
 def measure_configs(torch, peak: float, steps: int = 20, names=None) -> dict:
-    """Each config: 3 warm-up steps, then `steps` steps, each timed alone with
-    CUDA events after a 256 MB L2 flush (so no step reads the previous step's
-    data from L2). Inputs are device-generated; the numerics of these configs
-    are pinned by the parity tests. Returns {name: figures}."""
+    """Each config, two ways, 3 warm-up steps first:
+      us_per_step  steps back to back over R independent copies of the config,
+                   stepped in turn, with R chosen so the copies' resident state
+                   together exceeds 3x the 126 MB L2: every step finds its own
+                   data evicted by the R-1 steps before it (inputs larger than
+                   L2), as in training, where the forward and backward passes
+                   run between two optimizer steps; CUDA events around all
+                   `steps` x R steps;
+      isolated_us  one step timed alone (CUDA events) after an L2 flush (a
+                   256 MB write followed by a 256 MB read, so the lines left in
+                   L2 are clean and the step is not charged for the flush's
+                   write-backs): the latency of a single cold step, launch
+                   included.
+    Inputs are device-generated; the numerics of these configs are pinned by
+    the parity tests. Returns {name: figures}."""
     import soar_b200 as sb
     specs = config_specs()
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+    sink = torch.empty(1, dtype=torch.float32, device="cuda")
     out = {}
     for name, c in specs.items():
         if names and name not in names:
             continue
+        n = sum(c["sizes"])
         dt = torch.bfloat16 if c["layout"] == "bf16_mixed" else torch.float32
-        ps = [(torch.randn(k, device="cuda") * 0.02).to(dt) for k in c["sizes"]]
-        gs = [(torch.randn(k, device="cuda") * (1e-3 * (65536.0 if c["scaler"] else 1.0))).to(dt)
-              for k in c["sizes"]]
-        wds = c["wd"] or [0.01] * len(ps)
-        groups = [sb.ParamGroup([p], w) for p, w in zip(ps, wds)]
-        opt = sb.AdamW(groups, sb.AdamWOptions(lr=1e-3), layout=c["layout"],
-                       max_grad_norm=c["clip"],
-                       loss_scaler=sb.LossScalerOptions(init_scale=65536.0) if c["scaler"]
-                       else None, grads=gs)
-        sched = sb.CosineAnnealingLR(opt, *c["cosine"]) if c["cosine"] else None
+        resident = n * 16                                   # param, grad, master/m/v
+        reps = max(1, -(-3 * 126_000_000 // resident))
+        copies = []
+        for _ in range(reps):
+            ps = [(torch.randn(k, device="cuda") * 0.02).to(dt) for k in c["sizes"]]
+            gs = [(torch.randn(k, device="cuda") * (1e-3 * (65536.0 if c["scaler"] else 1.0)))
+                  .to(dt) for k in c["sizes"]]
+            wds = c["wd"] or [0.01] * len(ps)
+            opt = sb.AdamW([sb.ParamGroup([p], w) for p, w in zip(ps, wds)],
+                           sb.AdamWOptions(lr=1e-3), layout=c["layout"],
+                           max_grad_norm=c["clip"],
+                           loss_scaler=sb.LossScalerOptions(init_scale=65536.0) if c["scaler"]
+                           else None, grads=gs)
+            sched = sb.CosineAnnealingLR(opt, *c["cosine"]) if c["cosine"] else None
+            copies.append((ps, gs, opt, sched))
         s = torch.cuda.Stream()
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(steps)]
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        iso = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(10)]
         with torch.cuda.stream(s):
             for _ in range(3):
-                opt.step(s)
-            for a, b in evs:
+                for _, _, opt, _ in copies:
+                    opt.step(s)
+            torch.cuda.synchronize()
+            a.record(s)
+            for _ in range(steps):
+                for _, _, opt, sched in copies:
+                    opt.step(s)
+                    if sched:
+                        sched.step()
+            b.record(s)
+            opt0 = copies[0][2]
+            for e0, e1 in iso:
                 flush.fill_(1.0)
-                a.record(s)
-                opt.step(s)
-                b.record(s)
-                if sched:
-                    sched.step()
+                torch.sum(flush, 0, out=sink)
+                e0.record(s)
+                opt0.step(s)
+                e1.record(s)
         torch.cuda.synchronize()
-        us = [a.elapsed_time(b) * 1e3 for a, b in evs]
-        n = sum(c["sizes"])
-        mean_us = statistics.mean(us)
-        gbs = BYTES_PER_PARAM * n / (mean_us * 1e-6) / 1e9
-        info = opt.info()
+        us = a.elapsed_time(b) * 1e3 / (steps * reps)
+        iso_us = [e0.elapsed_time(e1) * 1e3 for e0, e1 in iso]
+        gbs = BYTES_PER_PARAM * n / (us * 1e-6) / 1e9
+        info = opt0.info()
         out[name] = {"params": n, "tensors": len(c["sizes"]), "layout": c["layout"],
-                     "us_per_step": round(mean_us, 2), "us_median": round(statistics.median(us), 2),
-                     "gparams_s": round(n / (mean_us * 1e-6) / 1e9, 2),
+                     "kernel": opt0.kernel_path, "copies": reps,
+                     "us_per_step": round(us, 2), "gparams_s": round(n / (us * 1e-6) / 1e9, 2),
                      "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 3),
+                     "isolated_us": round(statistics.median(iso_us), 2),
+                     "isolated_frac": round(BYTES_PER_PARAM * n / (statistics.median(iso_us)
+                                                                   * 1e-6) / 1e9 / peak, 3),
                      "steps": steps, "final_step": info.step, "skipped": info.skipped}
-        if sched:
-            sched.close()
-        opt.close()
-        del ps, gs, opt
+        for _, _, opt, sched in copies:
+            if sched:
+                sched.close()
+            opt.close()
+        del copies
         torch.cuda.empty_cache()
-    out["_how"] = (f"each step timed alone (CUDA events) after an L2 flush "
-                   f"({L2_FLUSH_BYTES >> 20} MB write), 3 warm-up steps; frac of the measured "
-                   f"{peak:.0f} GB/s HBM copy at 28 B/param")
+    out["_how"] = ("us_per_step: steps back to back over `copies` independent copies of the "
+                   "config stepped in turn (together > 3x L2, so each step's data is cold); "
+                   "isolated_us: median of one step timed alone after an L2 flush (256 MB "
+                   f"write + 256 MB read); frac of the measured {peak:.0f} GB/s HBM copy at "
+                   "28 B/param")
     return out
 
 

@@ -234,6 +234,29 @@ SOAR_API int soar_optim_enable_ema(void* handle, float decay, void* stream);
    and bf16 params in the mixed layout). */
 SOAR_API int soar_optim_ema_apply_to(void* handle, void* stream);
 
+/* Gradient buffers that change between steps. The reference reads each
+   parameter's current grad() at every step (adamw.cpp:74-75, 80-85); this
+   optimizer binds gradient buffers when it is created, and a caller whose
+   gradients live in more than one buffer (double-buffered host uploads,
+   gradient accumulation into alternating buffers) registers each further set
+   once: soar_optim_add_grads takes one gradient pointer per tensor (NULL
+   exactly where the creating list had NULL; each with the same address
+   modulo 16 bytes as the first set's, which torch and cudaMalloc buffers of
+   one layout have) and returns the set's index in *out_set (the creating
+   list is set 0). soar_optim_use_grads makes a set the one that step,
+   clip_grad_norm and zero_grad use from the next call on: host-side, no
+   device work; kernels already enqueued keep the set they were launched
+   with. Each added set holds its own copy of the chunk tables on the device
+   (64 bytes per chunk of up to 16384 elements), freed by soar_optim_destroy. */
+SOAR_API int soar_optim_add_grads(void* handle, void* const* grads, int* out_set);
+SOAR_API int soar_optim_use_grads(void* handle, int set);
+
+/* Which update kernel this optimizer's steps launch (*out_path): 0 = the
+   bulk-copy pipeline (k_apply), 1 = the register-fed single-pass kernel for
+   short lists (k_apply_direct: at most 4 tensors with a vector part and at
+   most 16M elements (16 x 2^20), no weight EMA, AdamW). Both compute the same bits. */
+SOAR_API int soar_optim_kernel_path(void* handle, int* out_path);
+
 /* Device address of the live loss scale (fp32), for scaling the loss on the
    device without a host round trip. */
 SOAR_API int soar_optim_loss_scale_ptr(void* handle, float** out_ptr);

@@ -60,6 +60,30 @@ struct TensorRec {
     uint64_t numel;
     float wd;
     uint64_t state_off;  // element offset of this tensor's master/m/v slices
+    uint64_t vec_from;   // first element of the 16-byte-aligned vector part (numel: none)
+};
+
+// Lists of at most kDirectMaxRuns tensors with a vector part and at most this
+// many elements update with the register-fed kernel (k_apply_direct) instead
+// of the bulk-copy pipeline: there a step lasts a few to tens of
+// microseconds and the pipeline's set-up and drain are a large share of it.
+// Measured on B200 (one flat tensor, plain update): the direct kernel is
+// faster at 1M-16M elements in both layouts (1M fp32 back to back: 6.7 vs
+// 9.7 us; 8M: 39.5 vs 41.3 us) and the pipeline from 32M on.
+#ifndef SOAR_DIRECT_MAX_ELEMS
+#define SOAR_DIRECT_MAX_ELEMS (16ull << 20)
+#endif
+constexpr uint64_t kDirectMaxElems = SOAR_DIRECT_MAX_ELEMS;
+
+// One set of gradient buffers for the optimizer's tensors, with the chunk
+// tables (and direct-kernel runs) that point into it. Set 0 is the one given
+// at create time; more are added with soar_optim_add_grads.
+struct GradSet {
+    std::vector<void*> grads;
+    soarb::Chunk* chunks = nullptr;        // update table (device)
+    soarb::Chunk* sumsq_chunks = nullptr;  // norm-pass table (device)
+    soarb::DirectRuns druns{};
+    void* alloc = nullptr;                 // device block of an added set's tables
 };
 
 struct Optim {
@@ -97,6 +121,11 @@ struct Optim {
 
     int grid_sumsq = 1;
     int grid_apply = 1;
+    bool direct = false;         // update with k_apply_direct (short lists)
+    soarb::DirectRuns druns{};   // of the gradient set in use
+    int grid_direct = 1;
+    std::vector<GradSet> grad_sets;
+    int grad_set = 0;            // the set step / clip / zero_grad use
     uint32_t chunk_elems = soarb::kChunkElems;  // adaptive: see choose_chunk_elems
     std::vector<soarb::Chunk> host_chunks;
     // The norm pass and the in-place fp32 clip walk the table before the tail
@@ -211,9 +240,11 @@ void build_chunks(Optim& o) {
             t.state_off = align_up(cursor + e0_raw, align_elems) - e0_raw;
             h16 = std::min<uint64_t>(h16_raw, t.numel);
             e0 = std::min<uint64_t>(e0_raw, t.numel);
+            t.vec_from = h16;
         } else {
             // 256-byte aligned slice start, shifted by the param's element phase
             t.state_off = align_up(cursor, 64) + pphase;
+            t.vec_from = t.numel;
         }
         cursor = t.state_off + t.numel;
         if (!t.grad || t.numel == 0) continue;
@@ -333,6 +364,36 @@ bool chunks_valid(const Optim& o, std::string* why) {
     return true;
 }
 
+// The direct kernel's runs: the vector part [vec_from, numel) of every
+// tensor with a gradient (exactly the elements the table's vector chunks
+// cover), for the gradient buffers `grads`. Returns false when the list has
+// more runs than the kernel takes.
+bool build_direct_runs(const Optim& o, const std::vector<void*>& grads, soarb::DirectRuns* out) {
+    soarb::DirectRuns r{};
+    const size_t eb = elem_bytes(o);
+    uint64_t vecs = 0;
+    for (size_t i = 0; i < o.tensors.size(); ++i) {
+        const TensorRec& t = o.tensors[i];
+        if (!grads[i] || t.vec_from >= t.numel) continue;
+        if (r.n_runs == soarb::kDirectMaxRuns) return false;
+        soarb::DirectRun& d = r.run[r.n_runs];
+        d.param = static_cast<char*>(t.param) + t.vec_from * eb;
+        d.grad = static_cast<const char*>(grads[i]) + t.vec_from * eb;
+        d.master = o.mixed ? o.master + t.state_off + t.vec_from
+                           : static_cast<float*>(t.param) + t.vec_from;
+        d.m = o.m + t.state_off + t.vec_from;
+        d.v = o.v + t.state_off + t.vec_from;
+        d.n = t.numel - t.vec_from;
+        d.wd = t.wd;
+        r.start[r.n_runs] = vecs;
+        vecs += (d.n + 3) / 4;
+        ++r.n_runs;
+    }
+    r.start[r.n_runs] = vecs;
+    *out = r;
+    return true;
+}
+
 struct SgdParams {
     float momentum, dampening;
     bool nesterov;
@@ -369,7 +430,7 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
             delete o;
             return fail("tensor " + std::to_string(i) + ": pointer not aligned to its element size");
         }
-        o->tensors.push_back({d.param, d.grad, d.numel, d.weight_decay, 0});
+        o->tensors.push_back({d.param, d.grad, d.numel, d.weight_decay, 0, d.numel});
     }
 
     DeviceGuard g(o->device);
@@ -498,6 +559,27 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
         const int rc = upload_bias_table(*o, 1u << 16);
         if (rc != SOAR_OK) return cleanup(g_last_error);
     }
+    {
+        GradSet g0;
+        for (const TensorRec& t : o->tensors) g0.grads.push_back(t.grad);
+        g0.chunks = o->chunks;
+        g0.sumsq_chunks = o->sumsq_chunks;
+        uint64_t total = 0;
+        for (const TensorRec& t : o->tensors)
+            if (t.grad) total += t.numel;
+        o->direct = !o->sgd && total > 0 && total <= kDirectMaxElems &&
+                    build_direct_runs(*o, g0.grads, &g0.druns);
+        if (o->direct) {
+            const uint64_t vecs = g0.druns.start[g0.druns.n_runs];
+            const uint64_t per_cta = static_cast<uint64_t>(soarb::kDirectThreads) *
+                                     soarb::kDirectVecs;
+            const uint64_t want = std::max<uint64_t>(1, (vecs + per_cta - 1) / per_cta);
+            const uint64_t cap = static_cast<uint64_t>(sms) * soarb::occupancy_apply_direct(o->mixed);
+            o->grid_direct = static_cast<int>(std::min(want, cap));
+        }
+        o->druns = g0.druns;
+        o->grad_sets.push_back(std::move(g0));
+    }
     if ((e = cudaDeviceSynchronize()) != cudaSuccess)
         return cleanup(std::string("create: ") + cudaGetErrorString(e));
     *out = o;
@@ -550,8 +632,13 @@ int apply_impl(Optim& o, const double* parts, int n_parts, cudaStream_t s,
     if (rc != SOAR_OK) return rc;
     soarb::ApplyArgs a = apply_args(o, parts, n_parts);
     a.skip_if = skip_if;
-    SOAR_CUDA_TRY(soarb::launch_apply(o.mixed, o.chunks, o.n_chunks, o.n_vec, o.ctl, a,
-                                      o.grid_apply, s, ag, o.ema != nullptr, o.sgd, o.dyn));
+    if (o.direct && !ag && !o.ema) {
+        SOAR_CUDA_TRY(soarb::launch_apply_direct(o.mixed, o.druns, o.chunks, o.n_chunks, o.n_vec,
+                                                 o.ctl, a, o.grid_direct, s));
+    } else {
+        SOAR_CUDA_TRY(soarb::launch_apply(o.mixed, o.chunks, o.n_chunks, o.n_vec, o.ctl, a,
+                                          o.grid_apply, s, ag, o.ema != nullptr, o.sgd, o.dyn));
+    }
     o.host_calls += 1;
     o.pending_coef = 1.0f;
     return SOAR_OK;
@@ -702,6 +789,8 @@ SOAR_API int soar_optim_destroy(void* handle) {
         cudaFree(o->slab);
         if (o->bc) cudaFree(o->bc);
         if (o->ema) cudaFree(o->ema);
+        for (GradSet& gs : o->grad_sets)
+            if (gs.alloc) cudaFree(gs.alloc);
     }
     delete o;
     return SOAR_OK;
@@ -1148,6 +1237,75 @@ SOAR_API int soar_selftest_bounded_wait(uint64_t limit_ns, int device, int* out_
     if (e != cudaSuccess) return fail(std::string("selftest: ") + cudaGetErrorString(e));
     *out_timed_out = err;
     *out_waited_ns = ns;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_optim_add_grads(void* handle, void* const* grads, int* out_set) {
+    if (!handle || !grads || !out_set) return fail("null argument");
+    Optim& o = *as_optim(handle);
+    const GradSet& g0 = o.grad_sets.front();
+    const size_t eb = elem_bytes(o);
+    std::vector<void*> ng(grads, grads + o.tensors.size());
+    for (size_t i = 0; i < ng.size(); ++i) {
+        const uintptr_t a = reinterpret_cast<uintptr_t>(ng[i]);
+        const uintptr_t b = reinterpret_cast<uintptr_t>(g0.grads[i]);
+        if ((ng[i] == nullptr) != (b == 0))
+            return fail("tensor " + std::to_string(i) + ": gradient presence differs from the "
+                        "optimizer's first gradient set");
+        if (ng[i] && (a % eb || a % soarb::kVecBytes != b % soarb::kVecBytes))
+            return fail("tensor " + std::to_string(i) + ": gradient alignment (address modulo 16 "
+                        "bytes) differs from the optimizer's first gradient set");
+    }
+    // the tables of set 0 with every gradient pointer moved to the new buffers
+    auto moved = [&](std::vector<soarb::Chunk> tab) {
+        for (soarb::Chunk& c : tab) {
+            const char* old_base = static_cast<const char*>(g0.grads[c.tensor]);
+            c.grad = static_cast<const char*>(ng[c.tensor]) +
+                     (static_cast<const char*>(c.grad) - old_base);
+        }
+        return tab;
+    };
+    const std::vector<soarb::Chunk> up = moved(o.host_chunks), ns = moved(o.host_sumsq_chunks);
+    GradSet gs;
+    gs.grads = ng;
+    if (o.direct && !build_direct_runs(o, ng, &gs.druns)) return fail("internal: direct runs");
+    DeviceGuard g(o.device);
+    const size_t up_bytes = align_up(up.size() * sizeof(soarb::Chunk), kSlabAlign);
+    const size_t bytes = up_bytes + ns.size() * sizeof(soarb::Chunk);
+    SOAR_CUDA_TRY(cudaMalloc(&gs.alloc, std::max<size_t>(bytes, 64)));
+    gs.chunks = static_cast<soarb::Chunk*>(gs.alloc);
+    gs.sumsq_chunks = reinterpret_cast<soarb::Chunk*>(static_cast<char*>(gs.alloc) + up_bytes);
+    cudaError_t e = cudaMemcpy(gs.chunks, up.data(), up.size() * sizeof(soarb::Chunk),
+                               cudaMemcpyHostToDevice);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(gs.sumsq_chunks, ns.data(), ns.size() * sizeof(soarb::Chunk),
+                       cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(gs.alloc);
+        return fail(std::string("gradient-set tables: ") + cudaGetErrorString(e));
+    }
+    o.grad_sets.push_back(std::move(gs));
+    *out_set = static_cast<int>(o.grad_sets.size()) - 1;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_optim_use_grads(void* handle, int set) {
+    if (!handle) return fail("null handle");
+    Optim& o = *as_optim(handle);
+    if (set < 0 || set >= static_cast<int>(o.grad_sets.size())) return fail("bad gradient set");
+    const GradSet& gs = o.grad_sets[set];
+    o.chunks = gs.chunks;
+    o.sumsq_chunks = gs.sumsq_chunks;
+    o.druns = gs.druns;
+    for (size_t i = 0; i < o.tensors.size(); ++i) o.tensors[i].grad = gs.grads[i];
+    o.grad_set = set;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_optim_kernel_path(void* handle, int* out_path) {
+    if (!handle || !out_path) return fail("null argument");
+    const Optim& o = *as_optim(handle);
+    *out_path = (o.direct && !o.ema) ? 1 : 0;
     return SOAR_OK;
 }
 

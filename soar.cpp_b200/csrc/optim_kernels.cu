@@ -207,6 +207,79 @@ __device__ __forceinline__ float ema_elem(float sh, float w, const ApplyArgs& a)
     return __fadd_rn(__fmul_rn(a.ema_decay, sh), __fmul_rn(a.ema_omd, w));
 }
 
+// The step's decision, taken by one thread of every CTA from the same bits:
+// skip (a failed peer sync, or inf/NaN with the scaler on), the pre-clip norm
+// from the rank-ordered fp64 partial sums, the clip coefficient and the bias
+// corrections of the step count the step will have. Counters are only read
+// here and only written by the last CTA (commit_step).
+struct StepDecision {
+    StepCoeffs k;
+    uint64_t t;
+    float norm;
+    int skip;
+    int found;
+};
+
+__device__ __forceinline__ StepDecision decide_step(const ApplyArgs& a, const Ctl* ctl) {
+    StepDecision d;
+    d.skip = 0;
+    d.found = 0;
+    d.norm = 0.0f;
+    float coef = a.pending_coef;
+    if (a.skip_if && *a.skip_if) {
+        d.skip = 1;  // a peer failed to synchronise: no update (the error flag tells)
+    } else if (a.n_parts > 0) {
+        double s = 0.0;
+        for (int p = 0; p < a.n_parts; ++p) s += a.parts[p];
+        d.found = !isfinite(s);
+        d.norm = __double2float_rn(__dsqrt_rn(s));  // adamw.cpp:42
+        if (a.use_scaler && d.found) d.skip = 1;
+        // adamw.cpp:43-44: no eps, no min(1, .)
+        if (a.max_norm > 0.0f && d.norm > a.max_norm && d.norm > 1e-6f)
+            coef = __fdiv_rn(a.max_norm, d.norm);
+    }
+    d.t = ctl->t + (d.skip ? 0u : 1u);
+    const uint64_t ti = d.t < a.bc_len ? d.t : static_cast<uint64_t>(a.bc_len - 1);
+    const float2 bc = a.bc[ti];
+    d.k.inv = a.use_scaler ? __fdiv_rn(1.0f, ctl->scale) : 1.0f;
+    d.k.coef = coef;
+    d.k.step_size = __fdiv_rn(a.lr, bc.x);  // adamw.cpp:71
+    d.k.sqrt_bc2 = bc.y;
+    d.k.has_buf = ctl->t > 0;  // applied steps so far (skipped steps never fill buffers)
+    return d;
+}
+
+// Called by thread 0 of every CTA once the CTA is done: the last CTA to
+// arrive (every CTA has read the counters by then) commits the step count,
+// the bookkeeping and the loss-scaler update, and resets the tickets.
+__device__ __forceinline__ void commit_step(Ctl* ctl, const ApplyArgs& a, const StepDecision& d) {
+    __threadfence();
+    const unsigned prev = atomicAdd(&ctl->ticket_apply, 1u);
+    if (prev != gridDim.x - 1) return;
+    ctl->t = d.t;
+    ctl->last_norm = d.norm;
+    ctl->last_found_inf = d.found;
+    ctl->last_clip_coef = d.skip ? 1.0f : d.k.coef;
+    ctl->last_lr = a.lr;
+    if (d.skip) ctl->skipped += 1u;
+    if (a.use_scaler) {
+        if (d.skip) {
+            ctl->scale = __fmul_rn(ctl->scale, a.backoff);
+            ctl->tracker = 0;
+        } else {
+            const int32_t tr = ctl->tracker + 1;
+            if (tr == a.interval) {
+                ctl->scale = __fmul_rn(ctl->scale, a.growth);
+                ctl->tracker = 0;
+            } else {
+                ctl->tracker = tr;
+            }
+        }
+    }
+    ctl->grab = 0u;  // every CTA has stopped grabbing
+    ctl->ticket_apply = 0u;
+}
+
 // Elements [from, to) of a chunk, straight from global memory. With kAg the
 // updated params are also written into every peer's parameter buffer.
 template <bool kMixed, bool kAg, bool kEma, bool kSgd>
@@ -301,36 +374,12 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
     pdl_wait();
     pdl_trigger();
     if (threadIdx.x == 0) {
-        // Every CTA derives the same decision from the same bits; counters are
-        // only read here and only written by the last CTA below.
-        int skip = 0, found = 0;
-        float norm = 0.0f, coef = a.pending_coef;
-        if (a.skip_if && *a.skip_if) {
-            skip = 1;  // a peer failed to synchronise: no update (the error flag tells)
-        } else if (a.n_parts > 0) {
-            double s = 0.0;
-            for (int p = 0; p < a.n_parts; ++p) s += a.parts[p];
-            found = !isfinite(s);
-            norm = __double2float_rn(__dsqrt_rn(s));  // adamw.cpp:42
-            if (a.use_scaler && found) skip = 1;
-            // adamw.cpp:43-44: no eps, no min(1, .)
-            if (a.max_norm > 0.0f && norm > a.max_norm && norm > 1e-6f)
-                coef = __fdiv_rn(a.max_norm, norm);
-        }
-        const uint64_t t = ctl->t + (skip ? 0u : 1u);
-        const uint64_t ti = t < a.bc_len ? t : static_cast<uint64_t>(a.bc_len - 1);
-        const float2 bc = a.bc[ti];
-        StepCoeffs k;
-        k.inv = a.use_scaler ? __fdiv_rn(1.0f, ctl->scale) : 1.0f;
-        k.coef = coef;
-        k.step_size = __fdiv_rn(a.lr, bc.x);  // adamw.cpp:71
-        k.sqrt_bc2 = bc.y;
-        k.has_buf = ctl->t > 0;  // applied steps so far (skipped steps never fill buffers)
-        s_k = k;
-        s_skip = skip;
-        s_t = t;
-        s_norm = norm;
-        s_found = found;
+        const StepDecision d = decide_step(a, ctl);
+        s_k = d.k;
+        s_skip = d.skip;
+        s_t = d.t;
+        s_norm = d.norm;
+        s_found = d.found;
         s_err = 0;
         s_drain_err = 0;
         s_cfail[0] = s_cfail[1] = 0;
@@ -557,34 +606,159 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
         atomicOr(&ctl->error, 1);
     }
     if (threadIdx.x == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(&ctl->ticket_apply, 1u);
-        if (prev == gridDim.x - 1) {
-            // Last CTA: every CTA has read the counters; commit the step.
-            ctl->t = s_t;
-            ctl->last_norm = s_norm;
-            ctl->last_found_inf = s_found;
-            ctl->last_clip_coef = s_skip ? 1.0f : k.coef;
-            ctl->last_lr = a.lr;
-            if (s_skip) ctl->skipped += 1u;
-            if (a.use_scaler) {
-                if (s_skip) {
-                    ctl->scale = __fmul_rn(ctl->scale, a.backoff);
-                    ctl->tracker = 0;
-                } else {
-                    const int32_t tr = ctl->tracker + 1;
-                    if (tr == a.interval) {
-                        ctl->scale = __fmul_rn(ctl->scale, a.growth);
-                        ctl->tracker = 0;
-                    } else {
-                        ctl->tracker = tr;
-                    }
-                }
+        StepDecision d;
+        d.k = k;
+        d.t = s_t;
+        d.norm = s_norm;
+        d.skip = s_skip;
+        d.found = s_found;
+        commit_step(ctl, a, d);
+    }
+}
+
+// ---------------------------------------------------------------- K2 direct --
+
+// One 4-element vector of a run: element offset e, n_valid (1..4) elements.
+// Full vectors are 16-byte loads of the fp32 streams (8 bytes of bf16);
+// the partial last vector of a run is loaded lane by lane.
+template <bool kMixed>
+__device__ __forceinline__ void direct_load(const DirectRun& r, uint64_t e, uint32_t n_valid,
+                                            float4& g, float4& th, float4& m, float4& v) {
+    if (n_valid == 4) {
+        if constexpr (kMixed) {
+            const uint2 q = __ldg(reinterpret_cast<const uint2*>(
+                static_cast<const uint16_t*>(r.grad) + e));
+            g = make_float4(bf16_lo(q.x), bf16_hi(q.x), bf16_lo(q.y), bf16_hi(q.y));
+        } else {
+            g = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(r.grad) + e));
+        }
+        th = *reinterpret_cast<const float4*>(r.master + e);
+        m = *reinterpret_cast<const float4*>(r.m + e);
+        v = *reinterpret_cast<const float4*>(r.v + e);
+        return;
+    }
+    float gg[4] = {0.f, 0.f, 0.f, 0.f}, tt[4] = {0.f, 0.f, 0.f, 0.f},
+          mm[4] = {0.f, 0.f, 0.f, 0.f}, vv[4] = {0.f, 0.f, 0.f, 0.f};
+    for (uint32_t j = 0; j < n_valid; ++j) {
+        gg[j] = kMixed ? bf16_bits_to_f32(static_cast<const uint16_t*>(r.grad)[e + j])
+                       : static_cast<const float*>(r.grad)[e + j];
+        tt[j] = r.master[e + j];
+        mm[j] = r.m[e + j];
+        vv[j] = r.v[e + j];
+    }
+    g = make_float4(gg[0], gg[1], gg[2], gg[3]);
+    th = make_float4(tt[0], tt[1], tt[2], tt[3]);
+    m = make_float4(mm[0], mm[1], mm[2], mm[3]);
+    v = make_float4(vv[0], vv[1], vv[2], vv[3]);
+}
+
+template <bool kMixed>
+__device__ __forceinline__ void direct_store(const DirectRun& r, uint64_t e, uint32_t n_valid,
+                                             const float4& th, const float4& m, const float4& v) {
+    if (n_valid == 4) {
+        *reinterpret_cast<float4*>(r.master + e) = th;
+        *reinterpret_cast<float4*>(r.m + e) = m;
+        *reinterpret_cast<float4*>(r.v + e) = v;
+        if constexpr (kMixed) {
+            uint2 p;
+            p.x = pack_bf16x2_rn(th.x, th.y);
+            p.y = pack_bf16x2_rn(th.z, th.w);
+            *reinterpret_cast<uint2*>(static_cast<uint16_t*>(r.param) + e) = p;
+        }
+        return;
+    }
+    const float tt[4] = {th.x, th.y, th.z, th.w}, mm[4] = {m.x, m.y, m.z, m.w},
+                vv[4] = {v.x, v.y, v.z, v.w};
+    for (uint32_t j = 0; j < n_valid; ++j) {
+        r.master[e + j] = tt[j];
+        r.m[e + j] = mm[j];
+        r.v[e + j] = vv[j];
+        if constexpr (kMixed) static_cast<uint16_t*>(r.param)[e + j] = f32_to_bf16_rn(tt[j]);
+    }
+}
+
+// Register-fed AdamW step for short tensor lists (config 1, small config-5
+// sizes), where the bulk-copy pipeline's set-up (prologue, ring fill, drain)
+// is a large share of a step of a few microseconds. One pass: every thread
+// issues the loads of its kDirectVecs vectors (grad, master, m, v) before
+// the step decision is read, so the prologue's dependent reads (control
+// block, bias-correction table) overlap the data in flight; then the same
+// per-element arithmetic as k_apply (adamw_elem, explicitly rounded, the
+// reference's order) and plain 16-byte stores. With the grid sized to the
+// vectors, a list of a few million elements is a single wave. The run
+// pointers come from the kernel parameters: no descriptor read precedes the
+// data loads. Scalar chunks of the table (misaligned heads, mixed-phase
+// tensors) follow, as in k_apply.
+template <bool kMixed>
+__global__ void __launch_bounds__(kDirectThreads, kDirectMinBlocks)
+k_apply_direct(DirectRuns runs, const Chunk* __restrict__ chunks, int n_chunks, int n_vec,
+               Ctl* __restrict__ ctl, ApplyArgs a) {
+    __shared__ StepDecision s_d;
+    pdl_wait();
+    pdl_trigger();
+    const uint32_t tid = threadIdx.x;
+    const uint64_t total = runs.start[runs.n_runs];
+    const uint64_t per_pass = static_cast<uint64_t>(gridDim.x) * kDirectThreads * kDirectVecs;
+
+    // Vector vi -> run, element offset, valid elements (runs in kernel params).
+    auto locate = [&](uint64_t vi, int& r, uint64_t& e, uint32_t& nv) {
+        r = 0;
+        while (r + 1 < runs.n_runs && vi >= runs.start[r + 1]) ++r;
+        e = (vi - runs.start[r]) * 4u;
+        const uint64_t left = runs.run[r].n - e;
+        nv = left < 4u ? static_cast<uint32_t>(left) : 4u;
+    };
+
+    float4 g[kDirectVecs], th[kDirectVecs], m[kDirectVecs], v[kDirectVecs];
+    int rr[kDirectVecs];
+    uint64_t ee[kDirectVecs];
+    uint32_t nn[kDirectVecs];
+    auto load_pass = [&](uint64_t base) {
+#pragma unroll
+        for (int j = 0; j < kDirectVecs; ++j) {
+            const uint64_t vi = base + static_cast<uint64_t>(j) * kDirectThreads + tid;
+            nn[j] = 0;
+            if (vi < total) {
+                locate(vi, rr[j], ee[j], nn[j]);
+                direct_load<kMixed>(runs.run[rr[j]], ee[j], nn[j], g[j], th[j], m[j], v[j]);
             }
-            ctl->grab = 0u;  // every CTA has stopped grabbing
-            ctl->ticket_apply = 0u;
+        }
+    };
+
+    uint64_t base = static_cast<uint64_t>(blockIdx.x) * kDirectThreads * kDirectVecs;
+    load_pass(base);  // in flight while thread 0 reads the step decision
+    if (tid == 0) s_d = decide_step(a, ctl);
+    __syncthreads();
+    const StepCoeffs k = s_d.k;
+    if (!s_d.skip) {
+        for (;;) {
+#pragma unroll
+            for (int j = 0; j < kDirectVecs; ++j) {
+                if (!nn[j]) continue;
+                const DirectRun& r = runs.run[rr[j]];
+                const float lr_wd = __fmul_rn(a.lr, r.wd);
+                const bool has_wd = r.wd != 0.0f;
+                adamw_elem(th[j].x, m[j].x, v[j].x, prep_grad(g[j].x, k), a, k, lr_wd, has_wd);
+                adamw_elem(th[j].y, m[j].y, v[j].y, prep_grad(g[j].y, k), a, k, lr_wd, has_wd);
+                adamw_elem(th[j].z, m[j].z, v[j].z, prep_grad(g[j].z, k), a, k, lr_wd, has_wd);
+                adamw_elem(th[j].w, m[j].w, v[j].w, prep_grad(g[j].w, k), a, k, lr_wd, has_wd);
+                direct_store<kMixed>(r, ee[j], nn[j], th[j], m[j], v[j]);
+            }
+            base += per_pass;
+            if (base >= total) break;
+            load_pass(base);
+        }
+        // scalar chunks (misaligned heads, mixed-phase tensors)
+        const AgArgs none{};
+        for (int c = n_vec + static_cast<int>(blockIdx.x); c < n_chunks; c += gridDim.x) {
+            const Chunk ch = chunks[c];
+            apply_scalar<kMixed, false, false, false>(ch, 0, ch.n, tid, kDirectThreads, a, k,
+                                                      __fmul_rn(a.lr, ch.wd), ch.wd != 0.0f,
+                                                      none);
         }
     }
+    __syncthreads();
+    if (tid == 0) commit_step(ctl, a, s_d);
 }
 
 // ------------------------------------------------------------ small kernels --
@@ -726,6 +900,26 @@ cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, int n_ve
     kVariants[variant_index(mixed, ag != nullptr, ema, sgd, dyn)].launch(
         chunks, n_chunks, n_vec, ctl, args, grid, stream, ag ? *ag : none);
     return cudaGetLastError();
+}
+
+cudaError_t launch_apply_direct(bool mixed, const DirectRuns& runs, const Chunk* chunks,
+                                int n_chunks, int n_vec, Ctl* ctl, const ApplyArgs& args,
+                                int grid, cudaStream_t stream) {
+    const cudaError_t e =
+        mixed ? launch_pdl(k_apply_direct<true>, dim3(grid), dim3(kDirectThreads), 0, stream,
+                           runs, chunks, n_chunks, n_vec, ctl, args)
+              : launch_pdl(k_apply_direct<false>, dim3(grid), dim3(kDirectThreads), 0, stream,
+                           runs, chunks, n_chunks, n_vec, ctl, args);
+    return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+int occupancy_apply_direct(bool mixed) {
+    int n = 0;
+    if (mixed)
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply_direct<true>, kDirectThreads, 0);
+    else
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_apply_direct<false>, kDirectThreads, 0);
+    return n > 0 ? n : 1;
 }
 
 cudaError_t launch_scale_grads_f32(const Chunk* chunks, int n_chunks, float coef, int grid,

@@ -150,6 +150,30 @@ __host__ __device__ constexpr size_t apply_smem_bytes(bool mixed, bool ema = fal
     return stage_bytes(mixed, ema, sgd) * apply_stages(mixed, ema, sgd);
 }
 
+// Register-fed update for short lists (k_apply_direct): up to kDirectMaxRuns
+// runs of 16-byte-aligned elements (the vector part of each tensor), passed by
+// value in the kernel parameters, so a thread's addresses need no table read
+// before its loads. Vector index space: run r holds vectors [start[r],
+// start[r + 1]) of 4 elements each (the last one of a run may be partial).
+constexpr int kDirectMaxRuns = 4;
+constexpr int kDirectThreads = 256;
+constexpr int kDirectVecs = 2;  // 4-element vectors per thread per pass
+constexpr int kDirectMinBlocks = 4;
+struct DirectRun {
+    void* param;        // fp32* or bf16*, at the run's first element
+    const void* grad;
+    float* master;      // == param in the fp32 layout
+    float* m;
+    float* v;
+    uint64_t n;         // elements in the run
+    float wd;
+};
+struct DirectRuns {
+    DirectRun run[kDirectMaxRuns];
+    uint64_t start[kDirectMaxRuns + 1];  // prefix sums of the runs' vector counts
+    int n_runs;
+};
+
 // Launchers (optim_kernels.cu). Each returns the launch status.
 cudaError_t launch_grad_sumsq(bool bf16, const Chunk* chunks, int n_chunks, Ctl* ctl,
                               double* partials, int grid, int use_scaler, double* out,
@@ -162,6 +186,13 @@ cudaError_t launch_apply(bool mixed, const Chunk* chunks, int n_chunks, int n_ve
                          const ApplyArgs& args, int grid, cudaStream_t stream,
                          const AgArgs* ag = nullptr, bool ema = false, bool sgd = false,
                          bool dyn = false);
+// The register-fed update over `runs` plus the scalar chunks of the table
+// (chunks[n_vec, n_chunks)): the AdamW step of k_apply without EMA, SGD or
+// the fused all-gather.
+cudaError_t launch_apply_direct(bool mixed, const DirectRuns& runs, const Chunk* chunks,
+                                int n_chunks, int n_vec, Ctl* ctl, const ApplyArgs& args,
+                                int grid, cudaStream_t stream);
+int occupancy_apply_direct(bool mixed);
 cudaError_t launch_scale_grads_f32(const Chunk* chunks, int n_chunks, float coef, int grid,
                                    cudaStream_t stream);
 cudaError_t launch_bf16_to_f32(const uint16_t* src, float* dst, uint64_t n,

@@ -120,6 +120,9 @@ SIGNATURES: dict[str, tuple] = {
     "soar_selftest_bounded_wait": (C.c_int, [C.c_uint64, C.c_int, C.POINTER(C.c_int),
                                              C.POINTER(C.c_uint64)]),
     "soar_kernel_arch": (C.c_int, [C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "soar_optim_add_grads": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_int)]),
+    "soar_optim_use_grads": (C.c_int, [C.c_void_p, C.c_int]),
+    "soar_optim_kernel_path": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
     "soar_last_error": (C.c_char_p, []),
 }
 
@@ -412,6 +415,30 @@ class AdamW:
     def load_state(self, path, stream=None) -> None:
         _check(lib().soar_optim_load_state(self.handle, str(path).encode(),
                                            _stream_handle(stream)), "soar_optim_load_state")
+
+    def add_grads(self, grads) -> int:
+        """Registers another set of gradient buffers (one per tensor, in the
+        order the optimizer was created with; None where it had none) and
+        returns its index; the creating list is set 0."""
+        n = len(self.numel)
+        if len(grads) != n:
+            raise ValueError(f"{n} gradient buffers expected")
+        arr = (C.c_void_p * n)(*[None if g is None else g.data_ptr() for g in grads])
+        out = C.c_int()
+        _check(lib().soar_optim_add_grads(self.handle, arr, C.byref(out)), "soar_optim_add_grads")
+        self._grad_sets = getattr(self, "_grad_sets", []) + [list(grads)]  # keep them alive
+        return out.value
+
+    def use_grads(self, index: int) -> None:
+        """Makes gradient set `index` the one the next steps use."""
+        _check(lib().soar_optim_use_grads(self.handle, index), "soar_optim_use_grads")
+
+    @property
+    def kernel_path(self) -> str:
+        """'pipeline' (k_apply) or 'direct' (k_apply_direct)."""
+        out = C.c_int()
+        _check(lib().soar_optim_kernel_path(self.handle, C.byref(out)), "soar_optim_kernel_path")
+        return "direct" if out.value == 1 else "pipeline"
 
     def loss_scale_ptr(self) -> int:
         out = C.c_void_p()

@@ -103,3 +103,107 @@ def test_config5_2b_sampled(oracle_mod, cuda, layout):
         np.testing.assert_array_equal(got_p.view(np.uint32), port.params[0].view(np.uint32))
     np.testing.assert_array_equal(got[sb.STATE_M].view(np.uint32), port.m[0].view(np.uint32))
     np.testing.assert_array_equal(got[sb.STATE_V].view(np.uint32), port.v[0].view(np.uint32))
+
+
+def test_config3_full_1000_steps(oracle_mod, cuda):
+    """Config 3 as BASELINE.json states it: 50M bf16-mixed params in 400
+    tensors (one flat buffer, so most tensors start off the 16-byte boundary),
+    clip 1.0, loss scale 65536 with growth after 200 clean steps, +inf into one
+    seeded gradient element every 97th step, 1000 steps.
+
+    Gradients: four seeded sets of N(0, 1e-3) fp32 values, cycled (fresh on
+    consecutive steps), scaled by the live loss scale and rounded to bf16 on
+    the device each step. The scale is a power of two, so the unscaled bf16
+    gradient of a set is the same at every scale and the host knows each
+    set's fp64 sum of squares exactly. Checked against the oracle:
+      - the skip / loss-scale / step-count sequence of all 1000 steps, bit for
+        bit (skips at 97, 194, ..., 970: ten backoffs, no growth);
+      - every step's global norm, bit for bit with the host's fp64 norm;
+      - the final master / m / v / bf16 params on a 65K-element sample (and
+        every tensor's first and last element), replayed through the oracle
+        over the same 1000 steps, bit for bit."""
+    torch = cuda
+    case = cases.c3(steps=1000)
+    sizes = case.sizes
+    n = sum(sizes)
+    assert n == 50_000_000 and len(sizes) == 400
+    offs = np.concatenate([[0], np.cumsum(sizes)]).astype(np.int64)
+    p0 = case.params0()
+    flat_p0 = np.concatenate(p0)
+    params = torch.from_numpy(flat_p0.view(np.int16)).view(torch.bfloat16).cuda()
+    grads = torch.empty_like(params)
+    views_p = [params[offs[i]:offs[i + 1]] for i in range(400)]
+    views_g = [grads[offs[i]:offs[i + 1]] for i in range(400)]
+    opt = sb.AdamW([sb.ParamGroup([p], 0.01) for p in views_p], sb.AdamWOptions(lr=1e-3),
+                   layout="bf16_mixed", max_grad_norm=1.0,
+                   loss_scaler=sb.LossScalerOptions(init_scale=65536.0, growth_interval=200),
+                   grads=views_g)
+    gen = torch.Generator(device="cuda")
+    pool = []
+    for k in range(4):
+        gen.manual_seed(3000 + k)
+        pool.append(torch.randn(n, device="cuda", generator=gen) * 1e-3)
+    tmp = torch.empty(n, dtype=torch.float32, device="cuda")
+
+    # host side: each set's unscaled bf16 values (exact at every power-of-two
+    # scale) and their fp64 sum of squares, and the sample
+    rng = np.random.default_rng(33)
+    idx = np.unique(np.concatenate([rng.integers(0, n, 1 << 16), offs[:-1], offs[1:] - 1]))
+    unscaled = []
+    sumsq = []
+    for k in range(4):
+        u = oracle_mod.bf16_to_f32(oracle_mod.f32_to_bf16(pool[k].cpu().numpy()))
+        sumsq.append(float(np.sum(u.astype(np.float64) ** 2)))
+        unscaled.append(u[idx].copy())
+
+    def inject(t):
+        i = t % 400
+        j = int(rng_inj.integers(0, sizes[i]))
+        return int(offs[i] + j)
+
+    rng_inj = np.random.default_rng(97)
+    inf_at = {t: inject(t) for t in range(97, 1001, 97)}
+
+    dev_hist = []
+    scale = 65536.0
+    for t in range(1, 1001):
+        k = t % 4
+        torch.mul(pool[k], scale, out=tmp)
+        grads.copy_(tmp)                          # round to nearest even bf16
+        if t in inf_at:
+            grads[inf_at[t]] = float("inf")
+        opt.step()
+        info = opt.info()
+        dev_hist.append((info.step, info.skipped, info.loss_scale, info.grad_norm,
+                         info.found_inf))
+        scale = info.loss_scale
+    got_p = params.view(torch.int16)[torch.from_numpy(idx).cuda()].cpu().numpy().view(np.uint16)
+
+    def state(kind):
+        v = torch.cat([opt.state(i, kind) for i in range(400)])
+        return v[torch.from_numpy(idx).cuda()].cpu().numpy()
+
+    got = {"master": state(sb.STATE_MASTER), "m": state(sb.STATE_M), "v": state(sb.STATE_V)}
+    opt.close()
+
+    # the oracle over the same 1000 steps on the sample
+    cfg = oracle_mod.StepConfig(layout=1, lr=1e-3, max_norm=1.0, use_scaler=True,
+                                growth_interval=200)
+    g_s = np.zeros(idx.size, np.uint16)
+    ps = oracle_mod.PortShard([flat_p0[idx].copy()], [g_s], [0.01], cfg, init_scale=65536.0)
+    for t in range(1, 1001):
+        k = t % 4
+        s = np.float32(ps.state.scale)
+        g_s[:] = oracle_mod.f32_to_bf16(unscaled[k] * s)   # exact: s is a power of two
+        total = float("inf") if t in inf_at else sumsq[k]
+        ps.apply_sumsq(total)
+        d = dev_hist[t - 1]
+        assert (d[0], d[1], d[2]) == (ps.state.t, ps.state.skipped, ps.state.scale), \
+            f"step {t}: device {d[:3]} vs oracle {(ps.state.t, ps.state.skipped, ps.state.scale)}"
+        if t not in inf_at:
+            assert np.float32(d[3]) == np.float32(ps.state.last_norm), f"norm at step {t}"
+    assert ps.state.skipped == 10 and ps.state.t == 990
+    assert ps.state.scale == 65536.0 / 2 ** 10
+    np.testing.assert_array_equal(got_p, ps.params[0])
+    for key, want in (("master", ps.master[0]), ("m", ps.m[0]), ("v", ps.v[0])):
+        np.testing.assert_array_equal(got[key].view(np.uint32), want.view(np.uint32), key)
