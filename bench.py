@@ -357,7 +357,10 @@ def run_ours(args):
     fused = world > 1 and args.dp.startswith("fused")
     dev_sync = fused and args.dp == "fused"
     if fused:
-        z = dp.FusedZeroOneAdamW(n, BUCKET, make_opt, device=local, init_params=params,
+        z = dp.FusedZeroOneAdamW(n, BUCKET, sb.AdamWOptions(lr=1e-3, weight_decay=0.01),
+                                 max_grad_norm=1.0,
+                                 loss_scaler=sb.LossScalerOptions(init_scale=65536.0),
+                                 device=local, init_params=params,
                                  sync="device" if dev_sync else "nccl")
         del params, grads
         params, grads = z.params, z.grads

@@ -178,6 +178,18 @@ SOAR_API int soar_optim_step(void* handle, void* stream);
 SOAR_API int soar_optim_clip_grad_norm(void* handle, float max_norm, float* out_norm,
                                        void* stream);
 
+/* clip_grad_norm(max_norm) without the host round trip, for callers that
+   ignore its return value, as the reference's Trainer does
+   (src/engine/trainer.cpp:157): enqueues the global-norm pass on `stream`;
+   the next soar_optim_step on the handle (on the same stream) then clips by
+   max_norm from that norm -- coefficient max_norm/norm when norm > max_norm
+   and norm > 1e-6, exactly as clip_grad_norm -- applied in fp32 inside the
+   update (the gradient buffers are left untouched), and reuses the pass
+   instead of running its own (the loss scaler's skip decision comes from the
+   same sum). The pre-clip norm is the step's grad_norm (soar_optim_get_info,
+   _async). Gradients must not change between this call and the step. */
+SOAR_API int soar_optim_clip_grad_norm_async(void* handle, float max_norm, void* stream);
+
 /* Replaces AdamW::zero_grad() (adamw.cpp:20-26): zeroes every gradient. */
 SOAR_API int soar_optim_zero_grad(void* handle, void* stream);
 
@@ -344,6 +356,71 @@ SOAR_API int soar_zero1_step(void* zero1_handle, void* stream);
    out (synchronises the device). */
 SOAR_API int soar_zero1_error(void* zero1_handle, int* out_error);
 SOAR_API int soar_zero1_destroy(void* zero1_handle);
+
+/* ---- Data-parallel bootstrap in the library ---------------------------
+   No counterpart in the reference, which has no distributed code. One process
+   per GPU, any host language: the ranks share an NCCL communicator and build
+   the fused ZeRO-1 step over it without Python or torch.
+
+   Rank 0 calls soar_dp_unique_id and hands the 128 bytes to every other rank
+   over any host channel (a file, MPI, a TCP store); every rank then calls
+   soar_dp_init with its rank, the world size (1..8), the id and its CUDA
+   device. NCCL (libnccl.so.2) is loaded when soar_dp_unique_id or
+   soar_dp_init is first called; like ncclCommInitRank, soar_dp_init returns
+   once every rank has joined. */
+#define SOAR_DP_UNIQUE_ID_BYTES 128
+SOAR_API int soar_dp_unique_id(void* out_id);
+SOAR_API int soar_dp_init(int rank, int world, const void* unique_id, int device,
+                          void** out_comm);
+SOAR_API int soar_dp_destroy(void* comm);
+/* Stream-ordered barrier over the communicator (a 1-element all-reduce): it
+   completes on this GPU once every rank's earlier work on its stream has. */
+SOAR_API int soar_dp_barrier(void* comm, void* stream);
+/* All-gather of `count` fp64 values per rank (rank order), on `stream`. */
+SOAR_API int soar_dp_allgather_f64(void* comm, const double* d_send, double* d_recv,
+                                   uint64_t count, void* stream);
+
+/* The fused ZeRO-1 optimizer over the communicator (collective: every rank
+   calls it with the same n_params, bucket and options). Allocates this rank's
+   flat bf16 parameter and gradient buffers of n_params elements (IPC
+   symmetric: every rank opens every other rank's), copies init_params into
+   the parameter buffer (n_params bf16 values, host or device; NULL leaves the
+   zeros), gives rank r the r-th ceil(size / world) slice of every bucket of
+   `bucket` elements, and creates the bf16-mixed AdamW of those slices with
+   `opts` (layout SOAR_LAYOUT_BF16_MIXED, opts->device = the communicator's
+   device; every slice takes opts->weight_decay; its fp32 master starts from
+   the initial params). sync_mode SOAR_DP_SYNC_DEVICE synchronises the ranks
+   inside the kernels through flags in a signal block (no host collective in a
+   step); SOAR_DP_SYNC_NCCL issues small collectives between the launches.
+   A failure on any rank is reported on every rank (the others do not hang). */
+#define SOAR_DP_SYNC_DEVICE 0
+#define SOAR_DP_SYNC_NCCL 1
+SOAR_API int soar_dp_zero1_create(void* comm, uint64_t n_params, uint64_t bucket,
+                                  const soar_adamw_opts* opts, const void* init_params,
+                                  int sync_mode, void** out_handle);
+
+typedef struct soar_dp_zero1_info {
+    void* params;          /* this rank's flat bf16 parameter buffer (device), n_params */
+    void* grads;           /* this rank's flat bf16 gradient buffer: fill before a step */
+    void* optimizer;       /* the shard optimizer: a soar_optim_* handle (info, lr,
+                              checkpoint; owned by this object) */
+    void* zero1;           /* the soar_zero1_* handle (error flag; owned by this object) */
+    uint64_t n_params;
+    uint64_t shard_params; /* elements this rank owns */
+    int32_t rank;
+    int32_t world;
+} soar_dp_zero1_info;
+SOAR_API int soar_dp_zero1_get_info(void* handle, soar_dp_zero1_info* out);
+
+/* One data-parallel step on `stream`: every rank's gradient (in its buffer,
+   complete in stream order) is averaged over the ranks, the owned slices are
+   updated (unscale, norm, clip, AdamW, bf16 write-back, loss scaler) and
+   every rank's parameter buffer holds the whole updated model once the step
+   completes. The rank's owned slice of its gradient buffer is overwritten
+   with the average. Every rank calls it once per step. */
+SOAR_API int soar_dp_zero1_step(void* handle, void* stream);
+/* Collective: releases the buffers once no rank maps them any more. */
+SOAR_API int soar_dp_zero1_destroy(void* handle);
 
 /* Replaces CosineAnnealingLR (adamw.hpp:45-57, adamw.cpp:119-143): linear
    warmup, cosine decay to eta_min, eta_min past the end; each step() sets the

@@ -103,6 +103,13 @@ public:
         detail::check(soar_optim_clip_grad_norm(h_, max_norm, &n, stream), "clip_grad_norm");
         return n;
     }
+    // The same clip without the host round trip, for a caller that ignores the
+    // returned norm (the reference's Trainer, trainer.cpp:157): the next step()
+    // clips by max_norm; the norm is that step's info().grad_norm.
+    void clip_grad_norm_async(float max_norm, void* stream = nullptr) {
+        detail::check(soar_optim_clip_grad_norm_async(h_, max_norm, stream),
+                      "clip_grad_norm_async");
+    }
     void set_lr(float lr) noexcept { soar_optim_set_lr(h_, lr); }
     [[nodiscard]] float get_lr() const noexcept {
         float lr = 0.0f;
@@ -218,6 +225,10 @@ public:
         detail::check(soar_optim_clip_grad_norm(h_, max_norm, &n, stream), "clip_grad_norm");
         return n;
     }
+    void clip_grad_norm_async(float max_norm, void* stream = nullptr) {
+        detail::check(soar_optim_clip_grad_norm_async(h_, max_norm, stream),
+                      "clip_grad_norm_async");
+    }
     void set_lr(float lr) noexcept { soar_optim_set_lr(h_, lr); }
     [[nodiscard]] float get_lr() const noexcept {
         float lr = 0.0f;
@@ -251,6 +262,96 @@ public:
 
 private:
     void* h_{nullptr};
+};
+
+// ---- data parallel (no reference counterpart) ------------------------------
+
+// NCCL communicator of one process (one GPU) of a data-parallel job
+// (soar_dp_init). Rank 0 creates the unique id (unique_id()) and hands the
+// bytes to the other ranks over any host channel.
+class Communicator {
+public:
+    static std::vector<unsigned char> unique_id() {
+        std::vector<unsigned char> id(SOAR_DP_UNIQUE_ID_BYTES);
+        detail::check(soar_dp_unique_id(id.data()), "dp_unique_id");
+        return id;
+    }
+    Communicator(int rank, int world, const std::vector<unsigned char>& id, int device)
+        : device_(device) {
+        if (id.size() != SOAR_DP_UNIQUE_ID_BYTES) throw std::runtime_error("bad unique id size");
+        detail::check(soar_dp_init(rank, world, id.data(), device, &h_), "dp_init");
+    }
+    Communicator(Communicator&& o) noexcept
+        : h_(std::exchange(o.h_, nullptr)), device_(o.device_) {}
+    Communicator(const Communicator&) = delete;
+    Communicator& operator=(const Communicator&) = delete;
+    ~Communicator() {
+        if (h_) soar_dp_destroy(h_);
+    }
+    void barrier(void* stream = nullptr) { detail::check(soar_dp_barrier(h_, stream), "barrier"); }
+    [[nodiscard]] void* handle() const noexcept { return h_; }
+    [[nodiscard]] int device() const noexcept { return device_; }
+
+private:
+    void* h_{nullptr};
+    int device_;
+};
+
+// Fused ZeRO-1 AdamW over a Communicator (soar_dp_zero1_create): the flat bf16
+// parameter and gradient buffers of n_params elements are the library's;
+// fill grads() with this rank's gradient, call step() on every rank, and
+// params() holds the updated model on every rank. Collective to construct and
+// to destroy. The communicator must outlive it.
+class ZeroOneAdamW {
+public:
+    ZeroOneAdamW(Communicator& comm, uint64_t n_params, uint64_t bucket,
+                 AdamWOptions options = {}, AdamWExtOptions ext = {},
+                 const void* init_params = nullptr, int sync_mode = SOAR_DP_SYNC_DEVICE) {
+        soar_adamw_opts c;
+        soar_adamw_default_opts(&c);
+        c.lr = options.lr;
+        c.beta1 = options.beta1;
+        c.beta2 = options.beta2;
+        c.eps = options.eps;
+        c.weight_decay = options.weight_decay;
+        c.layout = SOAR_LAYOUT_BF16_MIXED;
+        c.max_grad_norm = ext.max_grad_norm;
+        c.use_loss_scaler = ext.use_loss_scaler ? 1 : 0;
+        c.init_scale = ext.init_scale;
+        c.growth_factor = ext.growth_factor;
+        c.backoff_factor = ext.backoff_factor;
+        c.growth_interval = ext.growth_interval;
+        c.device = comm.device();
+        detail::check(soar_dp_zero1_create(comm.handle(), n_params, bucket, &c, init_params,
+                                           sync_mode, &h_),
+                      "dp_zero1_create");
+        detail::check(soar_dp_zero1_get_info(h_, &info_), "dp_zero1_get_info");
+    }
+    ZeroOneAdamW(ZeroOneAdamW&& o) noexcept : h_(std::exchange(o.h_, nullptr)), info_(o.info_) {}
+    ZeroOneAdamW(const ZeroOneAdamW&) = delete;
+    ZeroOneAdamW& operator=(const ZeroOneAdamW&) = delete;
+    ~ZeroOneAdamW() {
+        if (h_) soar_dp_zero1_destroy(h_);
+    }
+    void step(void* stream = nullptr) { detail::check(soar_dp_zero1_step(h_, stream), "dp_step"); }
+    [[nodiscard]] void* params() const noexcept { return info_.params; }
+    [[nodiscard]] void* grads() const noexcept { return info_.grads; }
+    [[nodiscard]] uint64_t shard_params() const noexcept { return info_.shard_params; }
+    [[nodiscard]] soar_step_info info(void* stream = nullptr) const {
+        soar_step_info i{};
+        detail::check(soar_optim_get_info(info_.optimizer, &i, stream), "get_info");
+        return i;
+    }
+    [[nodiscard]] int error() const {
+        int e = 0;
+        detail::check(soar_zero1_error(info_.zero1, &e), "zero1_error");
+        return e;
+    }
+    void set_lr(float lr) noexcept { soar_optim_set_lr(info_.optimizer, lr); }
+
+private:
+    void* h_{nullptr};
+    soar_dp_zero1_info info_{};
 };
 
 }  // namespace soar::optim

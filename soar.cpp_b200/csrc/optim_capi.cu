@@ -95,6 +95,8 @@ struct Optim {
     soar_adamw_opts opts{};
     float lr = 1e-3f;
     float pending_coef = 1.0f;   // from a standalone clip_grad_norm (mixed layout)
+    float async_clip = 0.0f;     // > 0: clip_grad_norm_async enqueued the norm pass; the
+                                 // next step clips by this norm from Ctl::sumsq
     uint64_t host_calls = 0;     // step() calls issued: an upper bound of the device t
 
     std::vector<TensorRec> tensors;
@@ -570,9 +572,10 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
         o->direct = !o->sgd && total > 0 && total <= kDirectMaxElems &&
                     build_direct_runs(*o, g0.grads, &g0.druns);
         if (o->direct) {
+            // as many CTAs as are resident at once, fewer when the vectors do
+            // not fill them (one vector per thread)
             const uint64_t vecs = g0.druns.start[g0.druns.n_runs];
-            const uint64_t per_cta = static_cast<uint64_t>(soarb::kDirectThreads) *
-                                     soarb::kDirectVecs;
+            const uint64_t per_cta = static_cast<uint64_t>(soarb::kDirectThreads);
             const uint64_t want = std::max<uint64_t>(1, (vecs + per_cta - 1) / per_cta);
             const uint64_t cap = static_cast<uint64_t>(sms) * soarb::occupancy_apply_direct(o->mixed);
             o->grid_direct = static_cast<int>(std::min(want, cap));
@@ -593,7 +596,8 @@ int ensure_bias_table(Optim& o) {
     return upload_bias_table(o, static_cast<uint32_t>(want));
 }
 
-soarb::ApplyArgs apply_args(const Optim& o, const double* parts, int n_parts) {
+soarb::ApplyArgs apply_args(const Optim& o, const double* parts, int n_parts,
+                            float max_norm) {
     soarb::ApplyArgs a{};
     a.lr = o.lr;
     a.beta1 = o.opts.beta1;
@@ -602,7 +606,7 @@ soarb::ApplyArgs apply_args(const Optim& o, const double* parts, int n_parts) {
     // adamw.cpp:100-101 evaluate (1.0f - beta) in float on the host
     a.omb1 = 1.0f - o.opts.beta1;
     a.omb2 = 1.0f - o.opts.beta2;
-    a.max_norm = o.opts.max_grad_norm;
+    a.max_norm = max_norm;
     a.pending_coef = o.pending_coef;
     a.growth = o.opts.growth_factor;
     a.backoff = o.opts.backoff_factor;
@@ -626,11 +630,13 @@ soarb::ApplyArgs apply_args(const Optim& o, const double* parts, int n_parts) {
 }
 
 int apply_impl(Optim& o, const double* parts, int n_parts, cudaStream_t s,
-               const soarb::AgArgs* ag = nullptr, const int* skip_if = nullptr) {
+               const soarb::AgArgs* ag = nullptr, const int* skip_if = nullptr,
+               float max_norm = -1.0f) {
     if (n_parts < 0 || (n_parts > 0 && !parts)) return fail("bad partial sums");
     int rc = ensure_bias_table(o);
     if (rc != SOAR_OK) return rc;
-    soarb::ApplyArgs a = apply_args(o, parts, n_parts);
+    soarb::ApplyArgs a =
+        apply_args(o, parts, n_parts, max_norm >= 0.0f ? max_norm : o.opts.max_grad_norm);
     a.skip_if = skip_if;
     if (o.direct && !ag && !o.ema) {
         SOAR_CUDA_TRY(soarb::launch_apply_direct(o.mixed, o.druns, o.chunks, o.n_chunks, o.n_vec,
@@ -802,6 +808,12 @@ SOAR_API int soar_optim_step(void* handle, void* stream) {
     DeviceGuard g(o.device);
     if (!g.ok) return fail("cannot select the optimizer's device");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (o.async_clip > 0.0f) {
+        // clip_grad_norm_async left the norm pass's sum in Ctl::sumsq
+        const float max_norm = o.async_clip;
+        o.async_clip = 0.0f;
+        return apply_impl(o, &o.ctl->sumsq, 1, s, nullptr, nullptr, max_norm);
+    }
     const bool need_norm = o.opts.use_loss_scaler || o.opts.max_grad_norm > 0.0f;
     if (need_norm) {
         double* d_sumsq = &o.ctl->sumsq;
@@ -849,6 +861,17 @@ SOAR_API int soar_optim_clip_grad_norm(void* handle, float max_norm, float* out_
         }
     }
     *out_norm = total_norm;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_optim_clip_grad_norm_async(void* handle, float max_norm, void* stream) {
+    if (!handle) return fail("null handle");
+    if (!(max_norm > 0.0f)) return fail("max_norm must be > 0");
+    Optim& o = *as_optim(handle);
+    DeviceGuard g(o.device);
+    const int rc = sumsq_impl(o, &o.ctl->sumsq, static_cast<cudaStream_t>(stream));
+    if (rc != SOAR_OK) return rc;
+    o.async_clip = max_norm;
     return SOAR_OK;
 }
 

@@ -698,7 +698,11 @@ k_apply_direct(DirectRuns runs, const Chunk* __restrict__ chunks, int n_chunks, 
     pdl_trigger();
     const uint32_t tid = threadIdx.x;
     const uint64_t total = runs.start[runs.n_runs];
-    const uint64_t per_pass = static_cast<uint64_t>(gridDim.x) * kDirectThreads * kDirectVecs;
+    // Vector j of a pass is this thread's slot in the j-th grid-wide stripe,
+    // so every thread of the (fully resident) grid gets its share and
+    // consecutive threads read consecutive vectors.
+    const uint64_t stripe = static_cast<uint64_t>(gridDim.x) * kDirectThreads;
+    const uint64_t per_pass = stripe * kDirectVecs;
 
     // Vector vi -> run, element offset, valid elements (runs in kernel params).
     auto locate = [&](uint64_t vi, int& r, uint64_t& e, uint32_t& nv) {
@@ -716,7 +720,7 @@ k_apply_direct(DirectRuns runs, const Chunk* __restrict__ chunks, int n_chunks, 
     auto load_pass = [&](uint64_t base) {
 #pragma unroll
         for (int j = 0; j < kDirectVecs; ++j) {
-            const uint64_t vi = base + static_cast<uint64_t>(j) * kDirectThreads + tid;
+            const uint64_t vi = base + static_cast<uint64_t>(j) * stripe;
             nn[j] = 0;
             if (vi < total) {
                 locate(vi, rr[j], ee[j], nn[j]);
@@ -725,7 +729,7 @@ k_apply_direct(DirectRuns runs, const Chunk* __restrict__ chunks, int n_chunks, 
         }
     };
 
-    uint64_t base = static_cast<uint64_t>(blockIdx.x) * kDirectThreads * kDirectVecs;
+    uint64_t base = static_cast<uint64_t>(blockIdx.x) * kDirectThreads + tid;
     load_pass(base);  // in flight while thread 0 reads the step decision
     if (tid == 0) s_d = decide_step(a, ctl);
     __syncthreads();
@@ -745,7 +749,7 @@ k_apply_direct(DirectRuns runs, const Chunk* __restrict__ chunks, int n_chunks, 
                 direct_store<kMixed>(r, ee[j], nn[j], th[j], m[j], v[j]);
             }
             base += per_pass;
-            if (base >= total) break;
+            if (base - tid >= total) break;  // the CTA's lowest vector: all threads leave together
             load_pass(base);
         }
         // scalar chunks (misaligned heads, mixed-phase tensors)

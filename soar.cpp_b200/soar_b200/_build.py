@@ -14,7 +14,8 @@ LIBDIR = ROOT / "lib"
 LIB = LIBDIR / "libsoar_optim.so"
 INCLUDE = ROOT.parent / "include"
 
-SOURCES = ["optim_kernels.cu", "optim_capi.cu", "noalloc_sumsq.cu", "zero1.cu"]
+SOURCES = ["optim_kernels.cu", "optim_capi.cu", "noalloc_sumsq.cu", "zero1.cu",
+           "dp_bootstrap.cu"]
 HEADERS = ["optim_kernels.cuh", "pipeline.cuh"]
 # the bench-only NVLink probe: a library of its own, not part of the C-ABI
 PROBE_LIB = LIBDIR / "libsoar_probe.so"
@@ -29,6 +30,7 @@ NVCC_FLAGS = [
     "-fmad=false",
     "-Xcompiler", "-fPIC,-fvisibility=hidden,-O3",
     "-shared",
+    "-ldl",   # NCCL is opened with dlopen by the data-parallel bootstrap
 ]
 
 

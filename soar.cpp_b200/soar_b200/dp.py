@@ -22,12 +22,13 @@ Two drivers:
   `Comm` object (torch.distributed / NCCL by default; gloo with a CPU stand-in
   optimizer in the host-logic tests).
 * FusedZeroOneAdamW -- steps 1-2 are one kernel and steps 4-5 are one kernel
-  over peer memory (soar_zero1_*): the parameter and gradient buffers are
-  allocated by the library and opened by every rank through CUDA IPC. The
-  ranks synchronise either inside the kernels, through epoch flags in a
-  symmetric signal block (sync="device", no host collective in the step), or
-  through an 8-byte partial all-gather and two 4-byte barriers over NCCL
-  (sync="nccl").
+  over peer memory (soar_zero1_*), set up by the library's data-parallel
+  bootstrap (soar_dp_init / soar_dp_zero1_create, usable from C or C++
+  without Python): the parameter and gradient buffers are allocated by the
+  library and opened by every rank through CUDA IPC. The ranks synchronise
+  either inside the kernels, through epoch flags in a symmetric signal block
+  (sync="device", no host collective in the step), or through an 8-byte
+  partial all-gather and two 4-byte barriers over NCCL (sync="nccl").
 """
 from __future__ import annotations
 
@@ -180,93 +181,102 @@ class _DevView:
 
 class FusedZeroOneAdamW:
     """ZeRO-1 step with the reduce-scatter fused into the norm pass and the
-    all-gather fused into the update (see the module docstring).
+    all-gather fused into the update (see the module docstring): a thin
+    caller of the library's data-parallel bootstrap (soar_dp_init /
+    soar_dp_zero1_create), which allocates and exchanges the symmetric buffers,
+    plans the buckets and owns the shard optimizer. torch.distributed only
+    carries NCCL's 128-byte unique id from rank 0 to the other ranks.
 
     `params` / `grads` are flat bf16 CUDA tensors viewing library-owned
     symmetric buffers: fill `grads` with this rank's gradient before step();
     after step() `params` holds the updated full model on every rank. The
     rank's own slice of `grads` is overwritten with the reduced average.
-    make_optimizer(shard_params, shard_grads) -> soar_b200.AdamW (bf16_mixed).
-    init_params (n bf16 values, any device) is copied into `params` before the
-    optimizer is created, so its fp32 master weights start from them.
+    `options` / max_grad_norm / loss_scaler configure the bf16-mixed AdamW of
+    the owned slices (every slice takes options.weight_decay); init_params
+    (n bf16 values, any device) is copied into `params` before the optimizer
+    is created, so its fp32 master weights start from them.
 
     sync="device" (default) synchronises the ranks inside the kernels through
-    epoch flags in a small symmetric signal block (soar_zero1_step: no host
-    collective in the step); sync="nccl" issues the three synchronisation
-    points as small NCCL collectives between the launches.
-    """
+    epoch flags in a small symmetric signal block (no host collective in the
+    step); sync="nccl" issues the three synchronisation points as small NCCL
+    collectives between the launches (over the library's communicator).
+    close() is collective: every rank calls it."""
 
-    def __init__(self, n: int, bucket: int, make_optimizer, group=None, device: int | None = None,
-                 init_params=None, sync: str = "device"):
+    def __init__(self, n: int, bucket: int, options=None, *, max_grad_norm: float = 0.0,
+                 loss_scaler=None, group=None, device: int | None = None, init_params=None,
+                 sync: str = "device"):
         import ctypes as C
 
         import torch
         import torch.distributed as dist
 
         from . import optim as _o
+        if sync not in ("device", "nccl"):
+            raise ValueError("sync must be 'device' or 'nccl'")
         self.torch, self.dist, self.group = torch, dist, group
         self.lib = _o.lib()
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.device = torch.cuda.current_device() if device is None else device
         self.n = n
-        self.buckets = plan_buckets(n, bucket, self.world, self.rank)
-        self._local, self._peers, self.zero1 = [], [], None
-        if sync not in ("device", "nccl"):
-            raise ValueError("sync must be 'device' or 'nccl'")
         self.sync = sync
-        bases = {}
-        sizes = {"grads": 2 * n, "params": 2 * n}
-        if sync == "device":
-            sizes["signals"] = _o.ZERO1_SIGNAL_BYTES
-        for name, nbytes in sizes.items():
-            ptr = C.c_void_p()
-            handle = (C.c_ubyte * _o.IPC_HANDLE_BYTES)()
-            _o._check(self.lib.soar_ipc_alloc(nbytes, self.device, C.byref(ptr), handle),
-                      "soar_ipc_alloc")
-            self._local.append(ptr.value)
-            handles = [None] * self.world
-            if self.world > 1:
-                dist.all_gather_object(handles, bytes(handle), group=group)
-            else:
-                handles = [bytes(handle)]
-            row = []
-            for q, h in enumerate(handles):
-                if q == self.rank:
-                    row.append(ptr.value)
-                    continue
-                peer = C.c_void_p()
-                buf = (C.c_ubyte * _o.IPC_HANDLE_BYTES).from_buffer_copy(h)
-                _o._check(self.lib.soar_ipc_open(buf, self.device, C.byref(peer)), "soar_ipc_open")
-                self._peers.append(peer.value)
-                row.append(peer.value)
-            bases[name] = row
-        dev = f"cuda:{self.device}"
-        self.grads = torch.as_tensor(_DevView(bases["grads"][self.rank], n, "<i2"),
-                                     device=dev).view(torch.bfloat16)
-        self.params = torch.as_tensor(_DevView(bases["params"][self.rank], n, "<i2"),
-                                      device=dev).view(torch.bfloat16)
+        self.buckets = plan_buckets(n, bucket, self.world, self.rank)
+        self.handle = self.comm = None
+        # NCCL's unique id, from rank 0 to every rank over torch.distributed
+        uid = (C.c_ubyte * _o.DP_UNIQUE_ID_BYTES)()
+        if self.rank == 0:
+            _o._check(self.lib.soar_dp_unique_id(uid), "soar_dp_unique_id")
+        if self.world > 1:
+            box = [bytes(uid)]
+            src = dist.get_global_rank(group, 0) if group is not None else 0
+            dist.broadcast_object_list(box, src=src, group=group)
+            uid = (C.c_ubyte * _o.DP_UNIQUE_ID_BYTES).from_buffer_copy(box[0])
+        comm = C.c_void_p()
+        _o._check(self.lib.soar_dp_init(self.rank, self.world, uid, self.device, C.byref(comm)),
+                  "soar_dp_init")
+        self.comm = comm
+        options = options or _o.AdamWOptions()
+        o = _o.AdamWOpts()
+        self.lib.soar_adamw_default_opts(C.byref(o))
+        o.lr, o.beta1, o.beta2, o.eps = options.lr, options.beta1, options.beta2, options.eps
+        o.weight_decay = options.weight_decay
+        o.layout = _o.LAYOUT_BF16_MIXED
+        o.max_grad_norm = max_grad_norm
+        if loss_scaler is not None:
+            o.use_loss_scaler = 1
+            o.init_scale = loss_scaler.init_scale
+            o.growth_factor = loss_scaler.growth_factor
+            o.backoff_factor = loss_scaler.backoff_factor
+            o.growth_interval = loss_scaler.growth_interval
+        o.device = self.device
+        init = None
         if init_params is not None:
-            self.params.copy_(init_params)
+            init_params = init_params.contiguous()
+            init = init_params.data_ptr()
+        h = C.c_void_p()
+        rc = self.lib.soar_dp_zero1_create(comm, n, bucket, C.byref(o), init,
+                                           _o.DP_SYNC_DEVICE if sync == "device"
+                                           else _o.DP_SYNC_NCCL, C.byref(h))
+        if rc != 0:
+            msg = self.lib.soar_last_error().decode(errors="replace")
+            self.lib.soar_dp_destroy(comm)
+            self.comm = None
+            raise _o.SoarError(f"soar_dp_zero1_create failed: {msg}")
+        self.handle = h
+        info = _o.DpZero1Info()
+        _o._check(self.lib.soar_dp_zero1_get_info(h, C.byref(info)), "soar_dp_zero1_get_info")
+        dev = f"cuda:{self.device}"
+        self.grads = torch.as_tensor(_DevView(info.grads, n, "<i2"), device=dev).view(
+            torch.bfloat16)
+        self.params = torch.as_tensor(_DevView(info.params, n, "<i2"), device=dev).view(
+            torch.bfloat16)
         mine = [b for b in self.buckets if b.own_size > 0]
         self.shard_params = [self.params[b.own_start:b.own_start + b.own_size] for b in mine]
         self.shard_grads = [self.grads[b.own_start:b.own_start + b.own_size] for b in mine]
-        self.opt = make_optimizer(self.shard_params, self.shard_grads)
-        shards = (_o.Zero1Shard * max(1, len(mine)))()
-        for i, b in enumerate(mine):
-            shards[i].offset, shards[i].count, shards[i].tensor = b.own_start, b.own_size, i
-        gb = (C.c_void_p * self.world)(*bases["grads"])
-        pb = (C.c_void_p * self.world)(*bases["params"])
-        h = C.c_void_p()
-        _o._check(self.lib.soar_zero1_create(self.opt.handle, self.rank, self.world, gb, pb,
-                                             shards, len(mine), C.byref(h)), "soar_zero1_create")
-        self.zero1 = h
-        if sync == "device":
-            sb = (C.c_void_p * self.world)(*bases["signals"])
-            _o._check(self.lib.soar_zero1_set_signals(h, sb), "soar_zero1_set_signals")
+        self.opt = _o.AdamW.borrow(info.optimizer, [b.own_size for b in mine], self.device)
+        self.zero1 = C.c_void_p(info.zero1)
         self.part = torch.zeros(1, dtype=torch.float64, device=dev)
         self.parts = torch.zeros(self.world, dtype=torch.float64, device=dev)
-        self.flag = torch.zeros(1, dtype=torch.float32, device=dev)
 
     def _stream(self):
         return self.torch.cuda.current_stream().cuda_stream
@@ -274,8 +284,9 @@ class FusedZeroOneAdamW:
     def barrier(self):
         """Stream-ordered barrier: completes on this GPU only after every
         rank's earlier work on its stream has completed."""
+        from . import optim as _o
         if self.world > 1:
-            self.dist.all_reduce(self.flag, group=self.group)
+            _o._check(self.lib.soar_dp_barrier(self.comm, self._stream()), "soar_dp_barrier")
 
     def reduce(self):
         from . import optim as _o
@@ -283,8 +294,11 @@ class FusedZeroOneAdamW:
                                                     self._stream()), "soar_zero1_reduce_sumsq")
 
     def gather_partials(self):
+        from . import optim as _o
         if self.world > 1:
-            self.dist.all_gather_into_tensor(self.parts, self.part, group=self.group)
+            _o._check(self.lib.soar_dp_allgather_f64(self.comm, self.part.data_ptr(),
+                                                      self.parts.data_ptr(), 1, self._stream()),
+                      "soar_dp_allgather_f64")
             return self.parts
         return self.part
 
@@ -295,14 +309,8 @@ class FusedZeroOneAdamW:
                   "soar_zero1_apply_allgather")
 
     def step(self):
-        if self.sync == "device":
-            from . import optim as _o
-            _o._check(self.lib.soar_zero1_step(self.zero1, self._stream()), "soar_zero1_step")
-            return
-        self.barrier()                        # every rank's gradients are complete
-        self.reduce()                         # reduce-scatter + sum of squares
-        self.update(self.gather_partials())   # update + all-gather
-        self.barrier()                        # every peer's parameter writes landed
+        from . import optim as _o
+        _o._check(self.lib.soar_dp_zero1_step(self.handle, self._stream()), "soar_dp_zero1_step")
 
     def error(self) -> int:
         import ctypes as C
@@ -313,20 +321,15 @@ class FusedZeroOneAdamW:
         return out.value
 
     def close(self):
-        if getattr(self, "zero1", None) is None and not getattr(self, "_local", None):
-            return
-        self.torch.cuda.synchronize(self.device)
-        if self.zero1 is not None:
-            self.lib.soar_zero1_destroy(self.zero1)
-            self.zero1 = None
-        if getattr(self, "opt", None) is not None:
+        """Collective: every rank calls it (no rank frees while a peer maps)."""
+        if getattr(self, "handle", None) is not None:
+            self.torch.cuda.synchronize(self.device)
             self.opt.close()
-        for p in self._peers:
-            self.lib.soar_ipc_close(p, self.device)
-        self._peers = []
-        for p in self._local:
-            self.lib.soar_ipc_free(p, self.device)
-        self._local = []
+            self.lib.soar_dp_zero1_destroy(self.handle)
+            self.handle = None
+        if getattr(self, "comm", None) is not None:
+            self.lib.soar_dp_destroy(self.comm)
+            self.comm = None
 
     def __del__(self):
         try:

@@ -80,6 +80,7 @@ SIGNATURES: dict[str, tuple] = {
     "soar_optim_step": (C.c_int, [C.c_void_p, C.c_void_p]),
     "soar_optim_clip_grad_norm": (C.c_int, [C.c_void_p, C.c_float, C.POINTER(C.c_float),
                                             C.c_void_p]),
+    "soar_optim_clip_grad_norm_async": (C.c_int, [C.c_void_p, C.c_float, C.c_void_p]),
     "soar_optim_zero_grad": (C.c_int, [C.c_void_p, C.c_void_p]),
     "soar_optim_set_lr": (C.c_int, [C.c_void_p, C.c_float]),
     "soar_optim_get_lr": (C.c_int, [C.c_void_p, C.POINTER(C.c_float)]),
@@ -120,6 +121,17 @@ SIGNATURES: dict[str, tuple] = {
     "soar_selftest_bounded_wait": (C.c_int, [C.c_uint64, C.c_int, C.POINTER(C.c_int),
                                              C.POINTER(C.c_uint64)]),
     "soar_kernel_arch": (C.c_int, [C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "soar_dp_unique_id": (C.c_int, [C.c_void_p]),
+    "soar_dp_init": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_int, C.POINTER(C.c_void_p)]),
+    "soar_dp_destroy": (C.c_int, [C.c_void_p]),
+    "soar_dp_barrier": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "soar_dp_allgather_f64": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64,
+                                        C.c_void_p]),
+    "soar_dp_zero1_create": (C.c_int, [C.c_void_p, C.c_uint64, C.c_uint64, C.c_void_p,
+                                       C.c_void_p, C.c_int, C.POINTER(C.c_void_p)]),
+    "soar_dp_zero1_get_info": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "soar_dp_zero1_step": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "soar_dp_zero1_destroy": (C.c_int, [C.c_void_p]),
     "soar_optim_add_grads": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_int)]),
     "soar_optim_use_grads": (C.c_int, [C.c_void_p, C.c_int]),
     "soar_optim_kernel_path": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
@@ -127,6 +139,14 @@ SIGNATURES: dict[str, tuple] = {
 }
 
 IPC_HANDLE_BYTES = 64
+DP_UNIQUE_ID_BYTES = 128
+DP_SYNC_DEVICE, DP_SYNC_NCCL = 0, 1
+
+
+class DpZero1Info(C.Structure):
+    _fields_ = [("params", C.c_void_p), ("grads", C.c_void_p), ("optimizer", C.c_void_p),
+                ("zero1", C.c_void_p), ("n_params", C.c_uint64), ("shard_params", C.c_uint64),
+                ("rank", C.c_int32), ("world", C.c_int32)]
 ZERO1_SIGNAL_BYTES = 4096
 
 
@@ -306,7 +326,23 @@ class AdamW:
         _check(create_fn(descs, n, C.byref(o), C.byref(h)), create_name)
         self.handle = h
 
+    @classmethod
+    def borrow(cls, handle: int, numel: list[int], device: int, layout: str = "bf16_mixed"):
+        """A view of an optimizer another object owns (the shard optimizer of
+        soar_dp_zero1_create): every method but close(), which does nothing."""
+        self = cls.__new__(cls)
+        self.handle = C.c_void_p(handle)
+        self.numel = list(numel)
+        self.device = device
+        self.layout = {"fp32": LAYOUT_FP32, "bf16_mixed": LAYOUT_BF16_MIXED}[layout]
+        self.params, self.grads, self.weight_decays = [], [], []
+        self._borrowed = True
+        return self
+
     def close(self):
+        if getattr(self, "_borrowed", False):
+            self.handle = None
+            return
         if getattr(self, "handle", None):
             lib().soar_optim_destroy(self.handle)
             self.handle = None
@@ -331,6 +367,13 @@ class AdamW:
                                                _stream_handle(stream)),
                "soar_optim_clip_grad_norm")
         return out.value
+
+    def clip_grad_norm_async(self, max_norm: float, stream=None) -> None:
+        """clip_grad_norm without the host round trip: the next step() clips
+        by max_norm from the norm computed here (grads left untouched)."""
+        _check(lib().soar_optim_clip_grad_norm_async(self.handle, max_norm,
+                                                      _stream_handle(stream)),
+               "soar_optim_clip_grad_norm_async")
 
     def set_lr(self, lr: float) -> None:
         _check(lib().soar_optim_set_lr(self.handle, lr), "soar_optim_set_lr")

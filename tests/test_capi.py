@@ -135,7 +135,7 @@ def test_ctypes_structs_match_the_c_layout(tmp_path):
         pytest.skip("no C compiler")
     pairs = [("soar_tensor_desc", optim.TensorDesc), ("soar_adamw_opts", optim.AdamWOpts),
              ("soar_sgd_opts", optim.SGDOpts), ("soar_step_info", optim.StepInfo),
-             ("soar_zero1_shard", optim.Zero1Shard)]
+             ("soar_zero1_shard", optim.Zero1Shard), ("soar_dp_zero1_info", optim.DpZero1Info)]
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "soar_optim.h"',
              "int main(void) {"]
     for cname, py in pairs:

@@ -166,14 +166,11 @@ def _fused_worker(rank, world, port, q, sync="nccl"):
     try:
         bf = lambda a: torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).cuda()
         p0 = bf(synth.to_bf16_bits(synth.normal(synth.seed_of(51), N, 0.02)))
-
-        def make(sp, sg):
-            return sb.AdamW([sb.ParamGroup(sp, 0.01)], layout="bf16_mixed", max_grad_norm=1.0,
-                            loss_scaler=sb.LossScalerOptions(init_scale=1024.0,
-                                                             growth_interval=2),
-                            grads=sg, device=rank)
-
-        fz = dp.FusedZeroOneAdamW(N, BUCKET, make, device=rank, init_params=p0, sync=sync)
+        fz = dp.FusedZeroOneAdamW(N, BUCKET, sb.AdamWOptions(weight_decay=0.01),
+                                  max_grad_norm=1.0,
+                                  loss_scaler=sb.LossScalerOptions(init_scale=1024.0,
+                                                                   growth_interval=2),
+                                  device=rank, init_params=p0, sync=sync)
         scale = 1024.0
         reduced, hist = [], []
         own = lambda: [fz.grads[b.own_start:b.own_start + b.own_size].view(torch.int16).cpu()
@@ -286,11 +283,8 @@ def _absent_peer_worker(rank, world, port, q):
         bf = lambda a: torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).cuda()
         p0 = bf(synth.to_bf16_bits(synth.normal(synth.seed_of(51), N, 0.02)))
 
-        def make(sp, sg):
-            return sb.AdamW([sb.ParamGroup(sp, 0.01)], layout="bf16_mixed", grads=sg,
-                            device=rank)
-
-        fz = dp.FusedZeroOneAdamW(N, BUCKET, make, device=rank, init_params=p0, sync="device")
+        fz = dp.FusedZeroOneAdamW(N, BUCKET, sb.AdamWOptions(weight_decay=0.01), device=rank,
+                                  init_params=p0, sync="device")
         fz.grads.copy_(bf(_grads(rank, 1, 1.0)))
         dist.barrier()
         out = None
@@ -375,7 +369,8 @@ def _full_c4_worker(rank, world, port, q):
             return sb.AdamW([sb.ParamGroup(sp, 0.01)], layout="bf16_mixed", max_grad_norm=1.0,
                             loss_scaler=scaler, grads=sg, device=rank)
 
-        fz = dp.FusedZeroOneAdamW(N4, B4, make, device=rank, init_params=p0, sync="device")
+        fz = dp.FusedZeroOneAdamW(N4, B4, sb.AdamWOptions(weight_decay=0.01), max_grad_norm=1.0,
+                                  loss_scaler=scaler, device=rank, init_params=p0, sync="device")
         full = dp.plan_buckets(N4, B4, 1, 0)
         if rank == 0:
             ref_p = p0.clone()

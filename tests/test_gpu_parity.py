@@ -172,6 +172,45 @@ def test_standalone_clip_then_step_matches_fused(oracle_mod, cuda):
             np.testing.assert_array_equal(a, b)
 
 
+@pytest.mark.parametrize("sizes", [[1000, 37, 4096], [1000, 37, 4096, 70001, 5, 16385]],
+                         ids=["direct", "pipeline"])
+def test_async_clip_matches_fused_and_standalone(oracle_mod, cuda, sizes):
+    """clip_grad_norm_async(max) + step() equals the fused step with
+    max_grad_norm=max and the synchronous clip_grad_norm(max) + step(), bit for
+    bit, in both layouts and on both update kernels, with the loss scaler on
+    (its skip decision then comes from the async norm pass too); the
+    gradients are left untouched."""
+    torch = cuda
+    for layout in (0, 1):
+        wd = [0.01, 0.0, 0.05, 0.01, 0.0, 0.02][:len(sizes)]
+        kw = dict(grad_std=0.01, seed=12, use_scaler=layout == 1, init_scale=1024.0,
+                  inf_every=3 if layout == 1 else 0)
+        fused = GpuRun(torch, cases.Case("c", layout, sizes, wd, 5, max_norm=0.05, **kw))
+        plain_case = cases.Case("c", layout, sizes, wd, 5, **kw)
+        sync, asyn = GpuRun(torch, plain_case), GpuRun(torch, plain_case)
+        assert asyn.opt.kernel_path == fused.opt.kernel_path
+        scale = 1024.0
+        for t in range(1, 6):
+            fused.step(t, scale)
+            for run in (sync, asyn):
+                run.load_grads(plain_case.grads(t, scale))
+            sync.opt.clip_grad_norm(0.05)
+            sync.opt.step()
+            before = [g.clone() for g in asyn.grads if g is not None]
+            asyn.opt.clip_grad_norm_async(0.05)
+            asyn.opt.step()
+            after = [g for g in asyn.grads if g is not None]
+            assert all(torch.equal(a, b) for a, b in zip(before, after))
+            fi, si, ai = fused.opt.info(), sync.opt.info(), asyn.opt.info()
+            assert (ai.step, ai.skipped, ai.loss_scale, ai.grad_norm, ai.clip_coef) == \
+                (fi.step, fi.skipped, fi.loss_scale, fi.grad_norm, fi.clip_coef)
+            scale = fi.loss_scale
+        assert fused.opt.info().skipped >= (1 if layout == 1 else 0)
+        for a, b, c in zip(fused.params_host(), asyn.params_host(), sync.params_host()):
+            np.testing.assert_array_equal(a, b)
+            np.testing.assert_array_equal(a, c)
+
+
 def test_dp_split_api_matches_step(oracle_mod, cuda):
     """grad_sumsq + apply(1 partial) is exactly step()."""
     torch = cuda
