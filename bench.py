@@ -103,6 +103,11 @@ def parse():
     ap.add_argument("--configs", action="store_true",
                     help="configs 1-3 and config-5 sizes on one GPU, one JSON line each "
                          "(not the headline line)")
+    ap.add_argument("--emulate-world", type=int, default=0,
+                    help="run the fused data-parallel kernels of R ranks on ONE GPU (every "
+                         "rank's buffers local, ranks in stream order) with --params params: "
+                         "the small case an ncu capture of k_rs_sumsq / k_apply<all-gather> "
+                         "runs on (not the headline line)")
     ap.add_argument("--dp", default="fused", choices=["fused", "fused-nccl", "nccl"],
                     help="N>1: collectives fused into the kernels over peer memory, the ranks "
                          "synchronised by device-side flags (default) or by small NCCL "
@@ -512,17 +517,30 @@ def run_ours(args):
     if fused:
         z.close()
     del z
-    if comm:
-        torch.distributed.barrier(device_ids=[local])
-        torch.distributed.destroy_process_group()
     torch.cuda.empty_cache()
     peak, peak_kind = measured_peak_hbm()
     configs = None
-    if rank == 0 and world == 1 and not args.no_configs:
+    if not args.no_configs and (world == 1 or comm):
+        # N = 1: configs 1-3 and config 5; N > 1: config 5 as one replica per
+        # GPU (the update has no cross-GPU term without a reduce), max over ranks
+        def together():
+            torch.cuda.synchronize()
+            torch.distributed.barrier(device_ids=[local])
+
+        def reduce_max(x):
+            v = torch.tensor([x], dtype=torch.float64, device=dev)
+            torch.distributed.all_reduce(v, op=torch.distributed.ReduceOp.MAX)
+            return float(v[0])
+        names = None if world == 1 else [k for k in config_specs() if k.startswith("c5")]
         try:
-            configs = measure_configs(torch, peak, steps=20)
+            configs = measure_configs(torch, peak, steps=20, names=names,
+                                      together=together if comm else None,
+                                      reduce_max=reduce_max if comm else None, world=world)
         except Exception as ex:  # reported beside the headline, never a reason to lose it
             configs = {"error": str(ex)[:300]}
+    if comm:
+        torch.distributed.barrier(device_ids=[local])
+        torch.distributed.destroy_process_group()
     if rank != 0:
         return 0
     apply_bytes = BYTES_PER_PARAM * shard_params
@@ -947,7 +965,8 @@ def config_specs(sizes5=(1_000_000, 16_000_000, 256_000_000)):
     return specs
 
 
-def measure_configs(torch, peak: float, steps: int = 20, names=None) -> dict:
+def measure_configs(torch, peak: float, steps: int = 20, names=None, together=None,
+                    reduce_max=None, world: int = 1) -> dict:
     """Each config, two ways, 3 warm-up steps first:
       us_per_step  steps back to back over R independent copies of the config,
                    stepped in turn, with R chosen so the copies' resident state
@@ -962,7 +981,10 @@ def measure_configs(torch, peak: float, steps: int = 20, names=None) -> dict:
                    write-backs): the latency of a single cold step, launch
                    included.
     Inputs are device-generated; the numerics of these configs are pinned by
-    the parity tests. Returns {name: figures}."""
+    the parity tests. Under torchrun every rank measures its own replica
+    (`together` starts the ranks' timed regions together, `reduce_max` takes
+    the slowest rank's time) and Gparams/s counts all `world` replicas.
+    Returns {name: figures}."""
     import soar_b200 as sb
     specs = config_specs()
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
@@ -997,6 +1019,8 @@ def measure_configs(torch, peak: float, steps: int = 20, names=None) -> dict:
                 for _, _, opt, _ in copies:
                     opt.step(s)
             torch.cuda.synchronize()
+            if together is not None:
+                together()
             a.record(s)
             for _ in range(steps):
                 for _, _, opt, sched in copies:
@@ -1014,11 +1038,14 @@ def measure_configs(torch, peak: float, steps: int = 20, names=None) -> dict:
         torch.cuda.synchronize()
         us = a.elapsed_time(b) * 1e3 / (steps * reps)
         iso_us = [e0.elapsed_time(e1) * 1e3 for e0, e1 in iso]
+        if reduce_max is not None:
+            us = reduce_max(us)
         gbs = BYTES_PER_PARAM * n / (us * 1e-6) / 1e9
         info = opt0.info()
         out[name] = {"params": n, "tensors": len(c["sizes"]), "layout": c["layout"],
                      "kernel": opt0.kernel_path, "copies": reps,
-                     "us_per_step": round(us, 2), "gparams_s": round(n / (us * 1e-6) / 1e9, 2),
+                     "us_per_step": round(us, 2),
+                     "gparams_s": round(world * n / (us * 1e-6) / 1e9, 2),
                      "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 3),
                      "isolated_us": round(statistics.median(iso_us), 2),
                      "isolated_frac": round(BYTES_PER_PARAM * n / (statistics.median(iso_us)
@@ -1161,6 +1188,83 @@ def run_sweep(args):
     return 0
 
 
+def run_emulated_world(args):
+    """The fused ZeRO-1 kernels of R ranks on one GPU: every rank's flat bf16
+    gradient and parameter buffers and shard optimizer on this device, the
+    caller-synchronised entry points in stream order (rank 0..R-1
+    reduce-scatter + norm, then rank 0..R-1 update + all-gather), config 4's
+    hyperparameters. Each kernel moves through HBM exactly the bytes its
+    multi-GPU launch moves through NVLink plus local HBM, so a one-GPU ncu
+    capture gives the per-launch traffic of the multi-GPU kernels. Prints one
+    JSON line with the mean duration of each kernel over `--steps` steps."""
+    import ctypes as C
+
+    import torch
+
+    import soar_b200 as sb
+    from soar_b200 import dp
+    from soar_b200 import optim as _o
+    world, n = args.emulate_world, args.params
+    torch.cuda.set_device(0)
+    lib = _o.lib()
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(404)
+    p0 = (torch.randn(n, device="cuda", generator=gen) * 0.02).bfloat16()
+    grads = [(torch.randn(n, device="cuda", generator=gen) * (1e-3 * 65536.0)).bfloat16()
+             for _ in range(world)]
+    params = [p0.clone() for _ in range(world)]
+    gb = (C.c_void_p * world)(*[g.data_ptr() for g in grads])
+    pb = (C.c_void_p * world)(*[p.data_ptr() for p in params])
+    opts, handles = [], []
+    for r in range(world):
+        plan = [b for b in dp.plan_buckets(n, BUCKET, world, r) if b.own_size > 0]
+        opt = sb.AdamW([sb.ParamGroup([params[r][b.own_start:b.own_start + b.own_size]
+                                       for b in plan], 0.01)], sb.AdamWOptions(lr=1e-3),
+                       layout="bf16_mixed", max_grad_norm=1.0,
+                       loss_scaler=sb.LossScalerOptions(init_scale=65536.0),
+                       grads=[grads[r][b.own_start:b.own_start + b.own_size] for b in plan])
+        shards = (_o.Zero1Shard * max(1, len(plan)))()
+        for i, b in enumerate(plan):
+            shards[i].offset, shards[i].count, shards[i].tensor = b.own_start, b.own_size, i
+        h = C.c_void_p()
+        _o._check(lib.soar_zero1_create(opt.handle, r, world, gb, pb, shards, len(plan),
+                                        C.byref(h)), "soar_zero1_create")
+        opts.append(opt)
+        handles.append(h)
+    part = torch.zeros(world, dtype=torch.float64, device="cuda")
+    s = torch.cuda.current_stream()
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    rs_ms, ag_ms = [], []
+    for k in range(args.warmup + args.steps):
+        marks = [ev() for _ in range(2 * world + 1)]
+        marks[0].record(s)
+        for r in range(world):
+            _o._check(lib.soar_zero1_reduce_sumsq(handles[r], C.c_void_p(part.data_ptr() + 8 * r),
+                                                  C.c_void_p(s.cuda_stream)), "reduce")
+            marks[1 + r].record(s)
+        for r in range(world):
+            _o._check(lib.soar_zero1_apply_allgather(handles[r], C.c_void_p(part.data_ptr()),
+                                                     world, C.c_void_p(s.cuda_stream)), "update")
+            marks[1 + world + r].record(s)
+        torch.cuda.synchronize()
+        if k >= args.warmup:
+            rs_ms += [marks[r].elapsed_time(marks[r + 1]) for r in range(world)]
+            ag_ms += [marks[world + r].elapsed_time(marks[world + r + 1]) for r in range(world)]
+    shard = n // world
+    print(json.dumps({"emulated_world": world, "params": n, "bucket": BUCKET,
+                      "shard_params": shard, "steps": args.steps,
+                      "k_rs_sumsq_ms": statistics.mean(rs_ms),
+                      "k_apply_allgather_ms": statistics.mean(ag_ms),
+                      "rs_bytes_per_launch": world * shard * 2 + shard * 2,
+                      "ag_bytes_per_launch": BYTES_PER_PARAM * shard + (world - 1) * shard * 2,
+                      "info": opts[0].info().as_dict()}), flush=True)
+    for h in handles:
+        lib.soar_zero1_destroy(h)
+    for o in opts:
+        o.close()
+    return 0
+
+
 def main():
     args = parse()
     if args.cpu_sample:
@@ -1173,6 +1277,8 @@ def main():
         return run_sweep(args)
     if args.configs:
         return run_configs(args)
+    if args.emulate_world:
+        return run_emulated_world(args)
     return run_ours(args)
 
 
