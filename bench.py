@@ -20,8 +20,9 @@ Rank 0 prints one JSON line. Besides the timed step it carries:
             step copies the rank's gradient in from pinned memory and its
             updated params out, on two copy streams so that the read-back of
             step s overlaps the upload of step s+1;
-  roofline  k_apply against the measured HBM copy peak at N = 1; the two
-            fused collective kernels against NVLink at N > 1 (HBM secondary);
+  roofline  k_apply against the measured HBM copy peak at N = 1; at N > 1 the
+            slower of the two fused kernels against its binding resource
+            (NVLink or HBM; both kernels under `rooflines`);
   parity    after the timed region, one more step checked against the CPU
             oracle on a sample of rank 0's shard, plus bit-identical params and
             counters on every rank;
@@ -552,8 +553,11 @@ def run_ours(args):
                              "launch of this command at N=1" if shard_params in
                              APPLY_TRAFFIC_BYTES else None,
            "algorithmic_bytes_per_launch": apply_bytes, "apply_ms": apply_ms_max}
-    roofline = hbm if world == 1 else nvlink_roofline(world, shard_params, phases,
-                                                      ms_max / args.steps)
+    per_kernel = None
+    if world == 1:
+        roofline = hbm
+    else:
+        roofline, per_kernel = dp_rooflines(world, shard_params, phases, peak)
     units = world * n * args.steps
     line = {
         "metric": METRIC,
@@ -599,7 +603,7 @@ def run_ours(args):
                        "grad_norm": info.grad_norm},
     }
     if world > 1:
-        line["roofline_hbm"] = hbm
+        line["rooflines"] = per_kernel
         line["nvlink_probe"] = probe
     if configs is not None:
         line["configs"] = configs
@@ -715,9 +719,10 @@ def parity_check(torch, np, z, world, rank, comm, g_pin, grads, params) -> dict:
         torch.cuda.synchronize()
         raw = grads.view(torch.int16)[flat].contiguous()
         raws = [raw]
-        if world > 1:
-            raws = [torch.empty_like(raw) for _ in range(world)]
-            tdist.all_gather(raws, raw)
+        if world > 1:  # moved as bf16 (the same bytes: NCCL has no int16)
+            got = [torch.empty_like(raw).view(torch.bfloat16) for _ in range(world)]
+            tdist.all_gather(got, raw.view(torch.bfloat16))
+            raws = [r.view(torch.int16) for r in got]
         info_b = z.opt.info()
         if rank == 0:
             st = {key: sample_state(kind) for kind, key in ((0, "master"), (1, "m"), (2, "v"))}
@@ -800,33 +805,53 @@ def parity_check(torch, np, z, world, rank, comm, g_pin, grads, params) -> dict:
     return out
 
 
-def nvlink_roofline(world, shard_params, phases, ms_per_step) -> dict:
-    """The binding roofline at N > 1: NVLink. Per step each rank pulls its
-    shard of every peer's gradient ((R-1) x shard x 2 B in, and as much out
-    while the peers pull theirs) and pushes its updated bf16 shard into every
-    peer ((R-1) x shard x 2 B out, as much in): 2 (R-1)/R x 2N bytes per
-    direction per rank. `achieved` divides them by the two collective phases'
-    times (phases_ms); `step_gbs` by the whole step."""
-    per_kernel = (world - 1) * shard_params * 2
-    nbytes = 2 * per_kernel
-    if "update+allgather" in phases:
-        t_rs, t_ag = phases["reduce_scatter+sumsq"], phases["update+allgather"]
-        kernels = "k_rs_sumsq + k_apply<all-gather>"
-    else:
-        t_rs, t_ag = phases["reduce_scatter"], phases["update"] + phases["param_allgather"]
-        kernels = "NCCL reduce-scatter + k_apply + NCCL all-gather"
-    achieved = nbytes / ((t_rs + t_ag) * 1e-3) / 1e9
-    step_gbs = nbytes / (ms_per_step * 1e-3) / 1e9
-    return {"bound": "nvlink", "kernel": kernels, "unit": "GB/s per direction per rank",
-            "achieved": achieved, "peak": NVLINK_PEER_COPY_GBS,
-            "peak_kind": "measured peer copy of this pool (per direction per GPU)",
-            "frac": achieved / NVLINK_PEER_COPY_GBS,
-            "peak_spec": NVLINK_SPEC_GBS, "frac_spec": achieved / NVLINK_SPEC_GBS,
-            "bytes_per_step": nbytes, "bytes_per_launch": per_kernel,
-            "phase_ms": {"reduce": t_rs, "update": t_ag},
-            "step_gbs": step_gbs, "step_frac": step_gbs / NVLINK_PEER_COPY_GBS,
-            "traffic": None,
-            "formula": "achieved = 2 x (R-1) x shard x 2 B / (reduce + update phase ms)"}
+def dp_rooflines(world, shard_params, phases, hbm_peak) -> tuple[dict, dict]:
+    """Rooflines of the data-parallel step's two kernels at N > 1, each against
+    its own binding resource (the larger of its two floors), from phases_ms:
+      k_rs_sumsq            NVLink: it pulls (R-1) x shard x 2 B from the peers
+                            while they pull as much from this GPU; HBM: own
+                            shard read + average written + the peers' pulls
+                            served, (R+1) x shard x 2 B;
+      k_apply<all-gather>   NVLink: it pushes (R-1) x shard x 2 B into the
+                            peers and receives as much; HBM: the 28 B/param
+                            update of the shard + the peers' pushes landing
+                            here, 28 x shard + (R-1) x shard x 2 B.
+    NVLink peak: the pool's measured peer copy, 770 GB/s per direction (spec
+    900); HBM peak: the measured copy. Returns (the slower kernel's roofline,
+    both)."""
+    nvl = (world - 1) * shard_params * 2
+    fused = "update+allgather" in phases
+    if fused:
+        times = {"k_rs_sumsq": phases["reduce_scatter+sumsq"],
+                 "k_apply<all-gather>": phases["update+allgather"]}
+    else:  # NCCL collectives around the kernels: time the update phase with them
+        times = {"k_rs_sumsq": phases["reduce_scatter"],
+                 "k_apply<all-gather>": phases["update"] + phases["param_allgather"]}
+    hbm_bytes = {"k_rs_sumsq": (world + 1) * shard_params * 2,
+                 "k_apply<all-gather>": BYTES_PER_PARAM * shard_params + nvl}
+    out = {}
+    for k, ms in times.items():
+        floors = {"nvlink": nvl / (NVLINK_PEER_COPY_GBS * 1e9),
+                  "hbm": hbm_bytes[k] / (hbm_peak * 1e9)}
+        bound = max(floors, key=floors.get)
+        nbytes = nvl if bound == "nvlink" else hbm_bytes[k]
+        peak = NVLINK_PEER_COPY_GBS if bound == "nvlink" else hbm_peak
+        achieved = nbytes / (ms * 1e-3) / 1e9
+        out[k] = {"bound": bound, "kernel": k, "achieved": achieved, "peak": peak,
+                  "peak_kind": "measured peer copy of this pool, per direction per GPU"
+                               if bound == "nvlink" else "measured HBM copy",
+                  "unit": "GB/s" + (" per direction per rank" if bound == "nvlink" else ""),
+                  "frac": achieved / peak, "bytes_per_launch": nbytes,
+                  "nvlink_bytes_per_direction": nvl, "hbm_bytes": hbm_bytes[k], "ms": ms,
+                  "floor_ms": {b: round(f * 1e3, 4) for b, f in floors.items()},
+                  "traffic": None}
+        if bound == "nvlink":
+            out[k]["peak_spec"] = NVLINK_SPEC_GBS
+            out[k]["frac_spec"] = achieved / NVLINK_SPEC_GBS
+        if not fused:
+            out[k]["kernel"] += " (NCCL around it)"
+    dominant = max(out.values(), key=lambda r: r["ms"])
+    return dominant, out
 
 
 def nvlink_probe_rates(torch, world, rank, local, shard_bytes) -> dict:

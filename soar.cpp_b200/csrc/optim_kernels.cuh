@@ -156,9 +156,18 @@ __host__ __device__ constexpr size_t apply_smem_bytes(bool mixed, bool ema = fal
 // before its loads. Vector index space: run r holds vectors [start[r],
 // start[r + 1]) of 4 elements each (the last one of a run may be partial).
 constexpr int kDirectMaxRuns = 4;
-constexpr int kDirectThreads = 256;
-constexpr int kDirectVecs = 2;  // 4-element vectors per thread per pass
-constexpr int kDirectMinBlocks = 4;
+#ifndef SOAR_DIRECT_THREADS
+#define SOAR_DIRECT_THREADS 256
+#endif
+#ifndef SOAR_DIRECT_VECS
+#define SOAR_DIRECT_VECS 2
+#endif
+#ifndef SOAR_DIRECT_MIN_BLOCKS
+#define SOAR_DIRECT_MIN_BLOCKS 4
+#endif
+constexpr int kDirectThreads = SOAR_DIRECT_THREADS;
+constexpr int kDirectVecs = SOAR_DIRECT_VECS;  // 4-element vectors per thread per pass
+constexpr int kDirectMinBlocks = SOAR_DIRECT_MIN_BLOCKS;
 struct DirectRun {
     void* param;        // fp32* or bf16*, at the run's first element
     const void* grad;

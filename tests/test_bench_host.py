@@ -117,14 +117,21 @@ def test_reference_sample_loads_nothing_of_the_package():
     assert "soar_b200" not in r.stdout and "soar.cpp_b200" not in r.stdout
 
 
-def test_nvlink_roofline_is_recomputable_from_the_phases():
+def test_dp_rooflines_are_recomputable_from_the_phases():
     phases = {"barrier": 0.01, "reduce_scatter+sumsq": 0.55, "partial_allgather": 0.02,
               "update+allgather": 0.57, "barrier2": 0.01}
     shard = 25_000_000
-    r = bench.nvlink_roofline(8, shard, phases, 1.2)
-    assert r["bound"] == "nvlink"
-    nbytes = 2 * 7 * shard * 2
-    assert r["bytes_per_step"] == nbytes
-    assert abs(r["achieved"] - nbytes / (1.12e-3) / 1e9) < 1e-6
-    assert abs(r["frac"] - r["achieved"] / bench.NVLINK_PEER_COPY_GBS) < 1e-12
-    assert abs(r["frac_spec"] - r["achieved"] / bench.NVLINK_SPEC_GBS) < 1e-12
+    dom, both = bench.dp_rooflines(8, shard, phases, 6552.0)
+    nvl = 7 * shard * 2
+    rs, ag = both["k_rs_sumsq"], both["k_apply<all-gather>"]
+    assert rs["bound"] == ag["bound"] == "nvlink" and dom is ag   # 8 GPUs: NVLink-bound
+    assert abs(rs["achieved"] - nvl / 0.55e-3 / 1e9) < 1e-6
+    assert abs(ag["frac"] - ag["achieved"] / bench.NVLINK_PEER_COPY_GBS) < 1e-12
+    assert abs(ag["frac_spec"] - ag["achieved"] / bench.NVLINK_SPEC_GBS) < 1e-12
+    # 2 GPUs: the update of a 100M shard is HBM-bound (28 B x 100M + 200 MB received)
+    phases2 = {"barrier": 0.016, "reduce_scatter+sumsq": 0.327, "partial_allgather": 0.014,
+               "update+allgather": 0.512, "barrier2": 0.019}
+    dom2, both2 = bench.dp_rooflines(2, 100_000_000, phases2, 6552.0)
+    assert both2["k_rs_sumsq"]["bound"] == "nvlink"
+    assert dom2["bound"] == "hbm" and dom2["kernel"] == "k_apply<all-gather>"
+    assert dom2["bytes_per_launch"] == 28 * 100_000_000 + 200_000_000
