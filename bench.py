@@ -60,6 +60,14 @@ UNIT = "Gparams/s"
 # bench's own command (2,801,499,392 read + 2,740,448,512 written). Reported
 # only for the workload it was measured on.
 APPLY_TRAFFIC_BYTES = {200_000_000: 5_541_141_760}
+# DRAM read + write per launch of the data-parallel kernels, per element of the
+# rank's shard, at 8 ranks: one-GPU ncu capture of the 8 ranks' kernels
+# (bench.py --emulate-world 8 --params 50000000: shard 6.25M elements, 8
+# launches of each kernel averaged). With every rank's buffers on one GPU, a
+# kernel's DRAM bytes are the per-GPU HBM bytes of its multi-GPU launch; the
+# writes that are still in L2 when the kernel ends are not in the count.
+DP_TRAFFIC_PER_ELEM = {8: {"k_rs_sumsq": (100_074_688 + 1_360_544) / 6_250_000,
+                           "k_apply<all-gather>": (87_747_232 + 122_004_608) / 6_250_000}}
 # NVLink references of this pool (per direction per GPU): the measured peer
 # copy and NVLink 5's specification.
 NVLINK_PEER_COPY_GBS = 770.0
@@ -843,8 +851,13 @@ def dp_rooflines(world, shard_params, phases, hbm_peak) -> tuple[dict, dict]:
                   "unit": "GB/s" + (" per direction per rank" if bound == "nvlink" else ""),
                   "frac": achieved / peak, "bytes_per_launch": nbytes,
                   "nvlink_bytes_per_direction": nvl, "hbm_bytes": hbm_bytes[k], "ms": ms,
-                  "floor_ms": {b: round(f * 1e3, 4) for b, f in floors.items()},
-                  "traffic": None}
+                  "floor_ms": {b: round(f * 1e3, 4) for b, f in floors.items()}}
+        per = DP_TRAFFIC_PER_ELEM.get(world, {}).get(k)
+        out[k]["traffic"] = round(per * shard_params) if per and fused else None
+        if out[k]["traffic"] is not None:
+            out[k]["traffic_source"] = ("HBM bytes per launch: one-GPU ncu capture of the "
+                                        f"{world} ranks' kernels (--emulate-world {world}, "
+                                        "shard 6.25M), scaled to this shard; compare hbm_bytes")
         if bound == "nvlink":
             out[k]["peak_spec"] = NVLINK_SPEC_GBS
             out[k]["frac_spec"] = achieved / NVLINK_SPEC_GBS
