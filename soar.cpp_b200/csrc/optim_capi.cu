@@ -542,10 +542,6 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
     ctl.scale = opts->use_loss_scaler ? opts->init_scale : 1.0f;
     ctl.last_clip_coef = 1.0f;
     ctl.last_lr = opts->lr;
-    {
-        bool conv = false;  // the first step's corrections, bc[1] (the table's own expressions)
-        ctl.bc_next = bias_table(opts->beta1, opts->beta2, 2, &conv)[1];
-    }
     if ((e = cudaMemcpy(o->ctl, &ctl, sizeof ctl, cudaMemcpyHostToDevice)) != cudaSuccess)
         return cleanup(std::string("control block upload: ") + cudaGetErrorString(e));
     if (o->mixed) {
@@ -593,10 +589,8 @@ int create_impl(const soar_tensor_desc* tensors, int n, const soar_adamw_opts* o
     return SOAR_OK;
 }
 
-// The table must hold bc[t + 1] for the step after the next one too: a step
-// stores the following step's corrections in Ctl::bc_next when it commits.
 int ensure_bias_table(Optim& o) {
-    if (o.bc_converged || o.host_calls + 2 < o.bc_len) return SOAR_OK;
+    if (o.bc_converged || o.host_calls + 1 < o.bc_len) return SOAR_OK;
     const uint64_t want = std::min<uint64_t>(static_cast<uint64_t>(o.bc_len) * 2, kBcCap);
     if (want <= o.bc_len) return fail("bias-correction table cap reached without converging");
     return upload_bias_table(o, static_cast<uint32_t>(want));
@@ -955,12 +949,10 @@ SOAR_API int soar_optim_set_counters(void* handle, uint64_t step, uint64_t skipp
     if (!handle) return fail("null handle");
     Optim& o = *as_optim(handle);
     DeviceGuard g(o.device);
-    o.host_calls = std::max(o.host_calls, step + skipped);
-    const int rc = ensure_bias_table(o);  // the table must reach bc[step + 1] first
-    if (rc != SOAR_OK) return rc;
     SOAR_CUDA_TRY(soarb::launch_set_counters(o.ctl, step, skipped, loss_scale, growth_tracker,
-                                             o.bc, o.bc_len, static_cast<cudaStream_t>(stream)));
-    return SOAR_OK;
+                                             static_cast<cudaStream_t>(stream)));
+    o.host_calls = std::max(o.host_calls, step + skipped);
+    return ensure_bias_table(o);
 }
 
 SOAR_API int soar_optim_state_ptr(void* handle, int index, int kind, void** out_ptr) {
@@ -1203,17 +1195,12 @@ SOAR_API int soar_optim_load_state(void* handle, const char* path, void* stream)
                                                     static_cast<uint16_t*>(t.param), t.numel, s));
         }
     }
+    SOAR_CUDA_TRY(soarb::launch_set_counters(o.ctl, ct.t, ct.skipped, ct.scale, ct.tracker, s));
     o.host_calls = std::max(ct.host_calls, ct.t + ct.skipped);
-    {
-        const int rc = ensure_bias_table(o);  // the table must reach bc[t + 1] first
-        if (rc != SOAR_OK) return rc;
-    }
-    SOAR_CUDA_TRY(soarb::launch_set_counters(o.ctl, ct.t, ct.skipped, ct.scale, ct.tracker, o.bc,
-                                             o.bc_len, s));
     o.lr = ct.lr;
     o.pending_coef = 1.0f;
     SOAR_CUDA_TRY(cudaStreamSynchronize(s));
-    return SOAR_OK;
+    return ensure_bias_table(o);
 }
 
 SOAR_API int soar_cosine_create(void* optim_handle, uint64_t total_steps, float eta_min,

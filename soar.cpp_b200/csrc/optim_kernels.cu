@@ -220,38 +220,17 @@ struct StepDecision {
     int found;
 };
 
-// The global-memory reads the decision needs, issued as loads whose results
-// are consumed later (decide_step), so a kernel can put them ahead of its
-// data loads.
-struct DecisionInputs {
-    uint64_t t;
-    float scale;
-    float2 bc;      // Ctl::bc_next
-    int skip_if;
-    double part0;   // parts[0] (the rest are read in decide_step)
-};
-
-__device__ __forceinline__ DecisionInputs read_decision_inputs(const ApplyArgs& a, const Ctl* ctl) {
-    DecisionInputs in;
-    in.t = ctl->t;
-    in.scale = ctl->scale;
-    in.bc = ctl->bc_next;
-    in.skip_if = a.skip_if ? *a.skip_if : 0;
-    in.part0 = a.n_parts > 0 ? a.parts[0] : 0.0;
-    return in;
-}
-
-__device__ __forceinline__ StepDecision decide_step(const ApplyArgs& a, const DecisionInputs& in) {
+__device__ __forceinline__ StepDecision decide_step(const ApplyArgs& a, const Ctl* ctl) {
     StepDecision d;
     d.skip = 0;
     d.found = 0;
     d.norm = 0.0f;
     float coef = a.pending_coef;
-    if (in.skip_if) {
+    if (a.skip_if && *a.skip_if) {
         d.skip = 1;  // a peer failed to synchronise: no update (the error flag tells)
     } else if (a.n_parts > 0) {
-        double s = 0.0 + in.part0;  // rank order, as the partial sums arrive
-        for (int p = 1; p < a.n_parts; ++p) s += a.parts[p];
+        double s = 0.0;
+        for (int p = 0; p < a.n_parts; ++p) s += a.parts[p];
         d.found = !isfinite(s);
         d.norm = __double2float_rn(__dsqrt_rn(s));  // adamw.cpp:42
         if (a.use_scaler && d.found) d.skip = 1;
@@ -259,27 +238,15 @@ __device__ __forceinline__ StepDecision decide_step(const ApplyArgs& a, const De
         if (a.max_norm > 0.0f && d.norm > a.max_norm && d.norm > 1e-6f)
             coef = __fdiv_rn(a.max_norm, d.norm);
     }
-    d.t = in.t + (d.skip ? 0u : 1u);
-    // the bias corrections of step in.t + 1 (the step count after this step
-    // when it is applied; unused when it is skipped)
-    const float2 bc = in.bc;
-    d.k.inv = a.use_scaler ? __fdiv_rn(1.0f, in.scale) : 1.0f;
+    d.t = ctl->t + (d.skip ? 0u : 1u);
+    const uint64_t ti = d.t < a.bc_len ? d.t : static_cast<uint64_t>(a.bc_len - 1);
+    const float2 bc = a.bc[ti];
+    d.k.inv = a.use_scaler ? __fdiv_rn(1.0f, ctl->scale) : 1.0f;
     d.k.coef = coef;
     d.k.step_size = __fdiv_rn(a.lr, bc.x);  // adamw.cpp:71
     d.k.sqrt_bc2 = bc.y;
-    d.k.has_buf = in.t > 0;  // applied steps so far (skipped steps never fill buffers)
+    d.k.has_buf = ctl->t > 0;  // applied steps so far (skipped steps never fill buffers)
     return d;
-}
-
-__device__ __forceinline__ StepDecision decide_step(const ApplyArgs& a, const Ctl* ctl) {
-    return decide_step(a, read_decision_inputs(a, ctl));
-}
-
-// bc[t + 1] of the table (its last entry past the end: the table runs until
-// both corrections are exactly 1).
-__device__ __forceinline__ float2 bias_next(const ApplyArgs& a, uint64_t t) {
-    const uint64_t i = t + 1 < a.bc_len ? t + 1 : static_cast<uint64_t>(a.bc_len - 1);
-    return a.bc[i];
 }
 
 // Called by thread 0 of every CTA once the CTA is done: the last CTA to
@@ -290,7 +257,6 @@ __device__ __forceinline__ void commit_step(Ctl* ctl, const ApplyArgs& a, const 
     const unsigned prev = atomicAdd(&ctl->ticket_apply, 1u);
     if (prev != gridDim.x - 1) return;
     ctl->t = d.t;
-    ctl->bc_next = bias_next(a, d.t);
     ctl->last_norm = d.norm;
     ctl->last_found_inf = d.found;
     ctl->last_clip_coef = d.skip ? 1.0f : d.k.coef;
@@ -654,9 +620,7 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
 
 // One 4-element vector of a run: element offset e, n_valid (1..4) elements.
 // Full vectors are 16-byte loads of the fp32 streams (8 bytes of bf16);
-// the partial last vector of a run is loaded lane by lane. In the mixed
-// layout the four bf16 gradients stay packed in g.x / g.y (their bits) until
-// direct_grad unpacks them: two registers per vector instead of four.
+// the partial last vector of a run is loaded lane by lane.
 template <bool kMixed>
 __device__ __forceinline__ void direct_load(const DirectRun& r, uint64_t e, uint32_t n_valid,
                                             float4& g, float4& th, float4& m, float4& v) {
@@ -664,7 +628,7 @@ __device__ __forceinline__ void direct_load(const DirectRun& r, uint64_t e, uint
         if constexpr (kMixed) {
             const uint2 q = __ldg(reinterpret_cast<const uint2*>(
                 static_cast<const uint16_t*>(r.grad) + e));
-            g = make_float4(__uint_as_float(q.x), __uint_as_float(q.y), 0.f, 0.f);
+            g = make_float4(bf16_lo(q.x), bf16_hi(q.x), bf16_lo(q.y), bf16_hi(q.y));
         } else {
             g = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(r.grad) + e));
         }
@@ -675,33 +639,17 @@ __device__ __forceinline__ void direct_load(const DirectRun& r, uint64_t e, uint
     }
     float gg[4] = {0.f, 0.f, 0.f, 0.f}, tt[4] = {0.f, 0.f, 0.f, 0.f},
           mm[4] = {0.f, 0.f, 0.f, 0.f}, vv[4] = {0.f, 0.f, 0.f, 0.f};
-    uint32_t gb[2] = {0u, 0u};
     for (uint32_t j = 0; j < n_valid; ++j) {
-        if constexpr (kMixed)
-            gb[j >> 1] |= static_cast<uint32_t>(static_cast<const uint16_t*>(r.grad)[e + j])
-                          << (16 * (j & 1));
-        else
-            gg[j] = static_cast<const float*>(r.grad)[e + j];
+        gg[j] = kMixed ? bf16_bits_to_f32(static_cast<const uint16_t*>(r.grad)[e + j])
+                       : static_cast<const float*>(r.grad)[e + j];
         tt[j] = r.master[e + j];
         mm[j] = r.m[e + j];
         vv[j] = r.v[e + j];
     }
-    g = kMixed ? make_float4(__uint_as_float(gb[0]), __uint_as_float(gb[1]), 0.f, 0.f)
-               : make_float4(gg[0], gg[1], gg[2], gg[3]);
+    g = make_float4(gg[0], gg[1], gg[2], gg[3]);
     th = make_float4(tt[0], tt[1], tt[2], tt[3]);
     m = make_float4(mm[0], mm[1], mm[2], mm[3]);
     v = make_float4(vv[0], vv[1], vv[2], vv[3]);
-}
-
-// The vector's gradient as four floats (unpacks the mixed layout's bf16 bits).
-template <bool kMixed>
-__device__ __forceinline__ float4 direct_grad(const float4& g) {
-    if constexpr (kMixed) {
-        const uint32_t x = __float_as_uint(g.x), y = __float_as_uint(g.y);
-        return make_float4(bf16_lo(x), bf16_hi(x), bf16_lo(y), bf16_hi(y));
-    } else {
-        return g;
-    }
 }
 
 template <bool kMixed>
@@ -765,76 +713,40 @@ k_apply_direct(DirectRuns runs, const Chunk* __restrict__ chunks, int n_chunks, 
         nv = left < 4u ? static_cast<uint32_t>(left) : 4u;
     };
 
-    // (a vector's run, offset and length are recomputed where they are used
-    // rather than kept live across the loads: registers are the limit here)
     float4 g[kDirectVecs], th[kDirectVecs], m[kDirectVecs], v[kDirectVecs];
+    int rr[kDirectVecs];
+    uint64_t ee[kDirectVecs];
+    uint32_t nn[kDirectVecs];
     auto load_pass = [&](uint64_t base) {
 #pragma unroll
         for (int j = 0; j < kDirectVecs; ++j) {
             const uint64_t vi = base + static_cast<uint64_t>(j) * stripe;
+            nn[j] = 0;
             if (vi < total) {
-                int r;
-                uint64_t e;
-                uint32_t nv;
-                locate(vi, r, e, nv);
-                direct_load<kMixed>(runs.run[r], e, nv, g[j], th[j], m[j], v[j]);
+                locate(vi, rr[j], ee[j], nn[j]);
+                direct_load<kMixed>(runs.run[rr[j]], ee[j], nn[j], g[j], th[j], m[j], v[j]);
             }
         }
     };
 
-    // The decision's reads are issued before the data loads, so they are not
-    // queued behind the grid's data requests: lanes 0-3 of warp 0 each load
-    // one 8-byte word (t; scale and tracker; bc_next; the first partial sum),
-    // which thread 0 gathers by shuffles once its own loads are in flight.
-    // (This kernel never runs with a peer-sync skip word.)
-    uint64_t word = 0;
-    if (tid < 4) {
-        const void* src = tid == 0   ? static_cast<const void*>(&ctl->t)
-                          : tid == 1 ? static_cast<const void*>(&ctl->scale)
-                          : tid == 2 ? static_cast<const void*>(&ctl->bc_next)
-                                     : (a.n_parts > 0 ? static_cast<const void*>(a.parts)
-                                                      : nullptr);
-        if (src) word = *static_cast<const uint64_t*>(src);
-    }
     uint64_t base = static_cast<uint64_t>(blockIdx.x) * kDirectThreads + tid;
-    load_pass(base);
-    if (tid < 32) {
-        const uint64_t w_t = __shfl_sync(0xffffffffu, word, 0);
-        const uint64_t w_scale = __shfl_sync(0xffffffffu, word, 1);
-        const uint64_t w_bc = __shfl_sync(0xffffffffu, word, 2);
-        const uint64_t w_part = __shfl_sync(0xffffffffu, word, 3);
-        if (tid == 0) {
-            DecisionInputs in;
-            in.t = w_t;
-            in.scale = __uint_as_float(static_cast<uint32_t>(w_scale));  // scale: low word
-            in.bc = make_float2(__uint_as_float(static_cast<uint32_t>(w_bc)),
-                                __uint_as_float(static_cast<uint32_t>(w_bc >> 32)));
-            in.skip_if = 0;
-            in.part0 = __longlong_as_double(static_cast<long long>(w_part));
-            s_d = decide_step(a, in);
-        }
-    }
+    load_pass(base);  // in flight while thread 0 reads the step decision
+    if (tid == 0) s_d = decide_step(a, ctl);
     __syncthreads();
     const StepCoeffs k = s_d.k;
     if (!s_d.skip) {
         for (;;) {
 #pragma unroll
             for (int j = 0; j < kDirectVecs; ++j) {
-                const uint64_t vi = base + static_cast<uint64_t>(j) * stripe;
-                if (vi >= total) continue;
-                int ri;
-                uint64_t e;
-                uint32_t nv;
-                locate(vi, ri, e, nv);
-                const DirectRun& r = runs.run[ri];
+                if (!nn[j]) continue;
+                const DirectRun& r = runs.run[rr[j]];
                 const float lr_wd = __fmul_rn(a.lr, r.wd);
                 const bool has_wd = r.wd != 0.0f;
-                const float4 gf = direct_grad<kMixed>(g[j]);
-                adamw_elem(th[j].x, m[j].x, v[j].x, prep_grad(gf.x, k), a, k, lr_wd, has_wd);
-                adamw_elem(th[j].y, m[j].y, v[j].y, prep_grad(gf.y, k), a, k, lr_wd, has_wd);
-                adamw_elem(th[j].z, m[j].z, v[j].z, prep_grad(gf.z, k), a, k, lr_wd, has_wd);
-                adamw_elem(th[j].w, m[j].w, v[j].w, prep_grad(gf.w, k), a, k, lr_wd, has_wd);
-                direct_store<kMixed>(r, e, nv, th[j], m[j], v[j]);
+                adamw_elem(th[j].x, m[j].x, v[j].x, prep_grad(g[j].x, k), a, k, lr_wd, has_wd);
+                adamw_elem(th[j].y, m[j].y, v[j].y, prep_grad(g[j].y, k), a, k, lr_wd, has_wd);
+                adamw_elem(th[j].z, m[j].z, v[j].z, prep_grad(g[j].z, k), a, k, lr_wd, has_wd);
+                adamw_elem(th[j].w, m[j].w, v[j].w, prep_grad(g[j].w, k), a, k, lr_wd, has_wd);
+                direct_store<kMixed>(r, ee[j], nn[j], th[j], m[j], v[j]);
             }
             base += per_pass;
             if (base - tid >= total) break;  // the CTA's lowest vector: all threads leave together
@@ -913,9 +825,8 @@ __global__ void k_step_done(SignalPtrs sig, int world, int rank, uint64_t epoch,
 }
 
 __global__ void k_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float scale,
-                               int32_t tracker, const float2* bc, uint32_t bc_len) {
+                               int32_t tracker) {
     ctl->t = t;
-    ctl->bc_next = bc[t + 1 < bc_len ? t + 1 : static_cast<uint64_t>(bc_len - 1)];
     ctl->skipped = skipped;
     ctl->scale = scale;
     ctl->tracker = tracker;
@@ -1040,9 +951,8 @@ cudaError_t launch_f32_to_bf16(const float* src, uint16_t* dst, uint64_t n,
 }
 
 cudaError_t launch_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float scale,
-                                int32_t tracker, const float2* bc, uint32_t bc_len,
-                                cudaStream_t stream) {
-    k_set_counters<<<1, 1, 0, stream>>>(ctl, t, skipped, scale, tracker, bc, bc_len);
+                                int32_t tracker, cudaStream_t stream) {
+    k_set_counters<<<1, 1, 0, stream>>>(ctl, t, skipped, scale, tracker);
     return cudaGetLastError();
 }
 

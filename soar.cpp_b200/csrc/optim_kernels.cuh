@@ -61,8 +61,7 @@ struct __align__(16) Chunk {
 };
 static_assert(sizeof(Chunk) == 64, "Chunk descriptor must stay one 64-byte line");
 
-// Device-resident step control block. The direct kernel reads `scale` (with
-// `tracker`), `t` and `bc_next` as 8-byte words: keep them 8-byte aligned. Persistent fields carry the optimizer's
+// Device-resident step control block. Persistent fields carry the optimizer's
 // counters across steps with no host round trip; the tickets implement the
 // single-pass grid reductions (last CTA finalises, then resets its ticket).
 struct __align__(64) Ctl {
@@ -79,9 +78,6 @@ struct __align__(64) Ctl {
     uint32_t ticket_apply;  // completion ticket of the update kernel
     int32_t error;          // nonzero: a pipeline wait timed out (the step is incomplete)
     uint32_t grab;          // chunks handed out so far by the running update (0 between launches)
-    float2 bc_next;         // bias corrections (1 - beta1^(t+1), sqrt(1 - beta2^(t+1))) of the
-                            // next applied step, stored by the step that set t (one read in the
-                            // next step's decision instead of a read of t, then of the table)
 };
 
 // Per-launch arguments of the update kernel.
@@ -213,8 +209,7 @@ cudaError_t launch_bf16_to_f32(const uint16_t* src, float* dst, uint64_t n,
 cudaError_t launch_f32_to_bf16(const float* src, uint16_t* dst, uint64_t n,
                                cudaStream_t stream);
 cudaError_t launch_set_counters(Ctl* ctl, uint64_t t, uint64_t skipped, float scale,
-                                int32_t tracker, const float2* bc, uint32_t bc_len,
-                                cudaStream_t stream);
+                                int32_t tracker, cudaStream_t stream);
 
 // Device-synchronised end of a data-parallel step: publishes done[rank] =
 // epoch into every peer's signal block, then waits (bounded) for every rank's.
