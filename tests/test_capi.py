@@ -79,6 +79,30 @@ def test_data_parallel_entry_points_reject_bad_arguments():
     assert lib.soar_zero1_error(None, None) == -1
 
 
+def test_data_parallel_bootstrap_rejects_bad_arguments():
+    """soar_dp_* argument checks run before NCCL or CUDA is touched (no GPU)."""
+    lib = sb.lib()
+    out = ctypes.c_void_p()
+    uid = (ctypes.c_ubyte * optim.DP_UNIQUE_ID_BYTES)()
+    assert lib.soar_dp_unique_id(None) == -1
+    assert lib.soar_dp_init(0, 2, None, 0, ctypes.byref(out)) == -1
+    assert b"null" in lib.soar_last_error()
+    assert lib.soar_dp_init(2, 2, uid, 0, ctypes.byref(out)) == -1      # rank outside the world
+    assert b"rank" in lib.soar_last_error()
+    assert lib.soar_dp_init(0, 9, uid, 0, ctypes.byref(out)) == -1      # at most 8 ranks
+    assert lib.soar_dp_destroy(None) == -1
+    assert lib.soar_dp_barrier(None, None) == -1
+    assert lib.soar_dp_allgather_f64(None, None, None, 1, None) == -1
+    opts = optim.AdamWOpts()
+    lib.soar_adamw_default_opts(ctypes.byref(opts))
+    assert lib.soar_dp_zero1_create(None, 10, 5, ctypes.byref(opts), None, 0,
+                                    ctypes.byref(out)) == -1
+    assert lib.soar_dp_zero1_step(None, None) == -1
+    assert lib.soar_dp_zero1_destroy(None) == -1
+    info = optim.DpZero1Info()
+    assert lib.soar_dp_zero1_get_info(None, ctypes.byref(info)) == -1
+
+
 def test_bench_probe_is_a_separate_library_and_checks_arguments():
     """The NVLink probe is a bench-only library (csrc/bench_probe.h), not an
     entry point of the optimizer's C-ABI; its argument checks need no GPU."""
