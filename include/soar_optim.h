@@ -258,7 +258,8 @@ SOAR_API int soar_optim_ema_apply_to(void* handle, void* stream);
    list is set 0). soar_optim_use_grads makes a set the one that step,
    clip_grad_norm and zero_grad use from the next call on: host-side, no
    device work; kernels already enqueued keep the set they were launched
-   with. Each added set holds its own copy of the chunk tables on the device
+   with, and a step captured into a CUDA graph keeps the set it was captured
+   with (capture one graph per set to alternate them). Each added set holds its own copy of the chunk tables on the device
    (64 bytes per chunk of up to 16384 elements), freed by soar_optim_destroy. */
 SOAR_API int soar_optim_add_grads(void* handle, void* const* grads, int* out_set);
 SOAR_API int soar_optim_use_grads(void* handle, int set);
