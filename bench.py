@@ -494,6 +494,11 @@ def run_ours(args):
         grads2 = torch.empty_like(grads)
         z.opt.add_grads([grads2[b.start:b.start + b.size] for b in z.buckets])
         grad_bufs, use_set = [grads, grads2], z.opt.use_grads
+    elif fused:
+        # the same with a second symmetric gradient buffer of the fused step
+        z.add_grads()
+        grads2 = z.grad_buffers[1]
+        grad_bufs, use_set = [z.grad_buffers[0], grads2], z.use_grads
     barrier()
     torch.cuda.synchronize()
     e2e_ms, e2e_copies = e2e_overlapped(torch, z.step, stream, grad_bufs, use_set, params,
@@ -599,8 +604,9 @@ def run_ours(args):
                 "transfers": "per rank: H2D of its full bf16 gradient from pinned memory, D2H "
                              "of its updated shard of the bf16 params (from a device snapshot); "
                              "two copy streams, so the read-back of step s overlaps the upload "
-                             "of step s+1" + (", which lands in a second gradient set while "
-                                              "step s runs" if world == 1 else ""),
+                             "of step s+1" + (", which lands in a second gradient buffer "
+                                              "while step s runs" if world == 1 or fused
+                                              else ""),
                 "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps,
                 "copies": e2e_copies},
         "clocks": clock_info,

@@ -420,6 +420,20 @@ SOAR_API int soar_dp_zero1_get_info(void* handle, soar_dp_zero1_info* out);
    completes. The rank's owned slice of its gradient buffer is overwritten
    with the average. Every rank calls it once per step. */
 SOAR_API int soar_dp_zero1_step(void* handle, void* stream);
+/* Further gradient buffers, so that the next step's gradient can be written
+   (an upload from the host, an accumulation) while a step still reads the
+   current one. soar_dp_zero1_add_grads (collective) allocates another
+   symmetric gradient buffer of n_params bf16 elements on every rank, with its
+   own signal block, and returns its index in *out_index (the buffer made by
+   soar_dp_zero1_create is 0). soar_dp_zero1_use_grads makes buffer `index` the
+   one the next soar_dp_zero1_step calls reduce (host-side; every rank must
+   use the same index for a step); soar_dp_zero1_get_info then reports it as
+   `grads` and `zero1`. soar_dp_zero1_grads gives this rank's buffer `index`.
+   A buffer may be rewritten once a step that read it has completed on this
+   rank's stream: by then every peer has finished reading it. */
+SOAR_API int soar_dp_zero1_add_grads(void* handle, int* out_index);
+SOAR_API int soar_dp_zero1_use_grads(void* handle, int index);
+SOAR_API int soar_dp_zero1_grads(void* handle, int index, void** out_grads);
 /* Collective: releases the buffers once no rank maps them any more. */
 SOAR_API int soar_dp_zero1_destroy(void* handle);
 

@@ -334,6 +334,22 @@ public:
         if (h_) soar_dp_zero1_destroy(h_);
     }
     void step(void* stream = nullptr) { detail::check(soar_dp_zero1_step(h_, stream), "dp_step"); }
+    // A further gradient buffer (collective); returns its index (the first is 0).
+    int add_grads() {
+        int k = -1;
+        detail::check(soar_dp_zero1_add_grads(h_, &k), "dp_zero1_add_grads");
+        return k;
+    }
+    // The buffer the next steps reduce (every rank the same index).
+    void use_grads(int index) {
+        detail::check(soar_dp_zero1_use_grads(h_, index), "dp_zero1_use_grads");
+        detail::check(soar_dp_zero1_get_info(h_, &info_), "dp_zero1_get_info");
+    }
+    [[nodiscard]] void* grads(int index) const {
+        void* p = nullptr;
+        detail::check(soar_dp_zero1_grads(h_, index, &p), "dp_zero1_grads");
+        return p;
+    }
     [[nodiscard]] void* params() const noexcept { return info_.params; }
     [[nodiscard]] void* grads() const noexcept { return info_.grads; }
     [[nodiscard]] uint64_t shard_params() const noexcept { return info_.shard_params; }

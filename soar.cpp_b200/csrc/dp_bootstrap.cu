@@ -161,12 +161,73 @@ struct DpZero1 {
     DpComm* comm;
     int sync_mode;
     uint64_t n = 0, shard = 0;
-    void* local[3] = {nullptr, nullptr, nullptr};  // grads, params, signals
+    void* local[3] = {nullptr, nullptr, nullptr};  // grads (set 0), params, signals (set 0)
+    std::vector<void*> extra;                       // further gradient buffers and signal blocks
     std::vector<void*> peers;                       // opened peer mappings
     void* optim = nullptr;
-    void* zero1 = nullptr;
+    std::vector<void*> zero1;                       // one fused-step handle per gradient set
+    std::vector<void*> grads;                       // this rank's buffer of each gradient set
+    int cur = 0;                                    // the set the next steps reduce
+    std::vector<void*> param_bases;                 // every rank's parameter buffer
+    std::vector<soar_zero1_shard> shards;
     double* d_part = nullptr;                       // sync mode 1: own partial + R partials
 };
+
+// Allocates `n` symmetric buffers of bytes[k] on every rank, exchanges their
+// IPC handles over the communicator and opens the peers' (collective; every
+// phase agreed on). bases[k][q] is rank q's buffer k as seen from here; the
+// local buffers go to `locals`, the peer mappings to z.peers.
+bool symmetric_alloc(DpZero1& z, int n, const size_t* bytes, std::vector<void*>* bases,
+                     std::vector<void*>& locals, std::string* why) {
+    DpComm& c = *z.comm;
+    std::vector<unsigned char> mine(static_cast<size_t>(n) * SOAR_IPC_HANDLE_BYTES);
+    bool ok = true;
+    for (int k = 0; k < n && ok; ++k) {
+        void* p = nullptr;
+        ok = soar_ipc_alloc(bytes[k], c.device, &p, mine.data() + k * SOAR_IPC_HANDLE_BYTES) ==
+             SOAR_OK;
+        if (ok) locals.push_back(p);
+        else *why = soar_last_error();
+    }
+    if (!agree(c, ok, why)) return false;
+    std::vector<unsigned char> all(static_cast<size_t>(c.world) * mine.size());
+    {
+        unsigned char* d_buf = nullptr;
+        cudaError_t e = cudaMalloc(&d_buf, all.size());
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(d_buf + c.rank * mine.size(), mine.data(), mine.size(),
+                                cudaMemcpyHostToDevice, c.stream);
+        ncclResult_t r = ncclSuccess;
+        if (e == cudaSuccess)
+            r = c.api->all_gather(d_buf + c.rank * mine.size(), d_buf, mine.size(), ncclUint8,
+                                  c.comm, c.stream);
+        if (e == cudaSuccess && r == ncclSuccess)
+            e = cudaMemcpyAsync(all.data(), d_buf, all.size(), cudaMemcpyDeviceToHost, c.stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c.stream);
+        if (d_buf) cudaFree(d_buf);
+        ok = e == cudaSuccess && r == ncclSuccess;
+        if (!ok) *why = "handle exchange failed";
+    }
+    for (int k = 0; k < n; ++k) bases[k].assign(c.world, nullptr);
+    for (int q = 0; q < c.world && ok; ++q) {
+        for (int k = 0; k < n && ok; ++k) {
+            if (q == c.rank) {
+                bases[k][q] = locals[locals.size() - n + k];
+                continue;
+            }
+            const unsigned char* h = all.data() + (q * n + k) * SOAR_IPC_HANDLE_BYTES;
+            void* p = nullptr;
+            ok = soar_ipc_open(h, c.device, &p) == SOAR_OK;
+            if (ok) {
+                z.peers.push_back(p);
+                bases[k][q] = p;
+            } else {
+                *why = soar_last_error();
+            }
+        }
+    }
+    return agree(c, ok, why);
+}
 
 // Releases what `z` holds. Collective (every rank calls it): no rank frees
 // its buffers while a peer may still map them.
@@ -174,9 +235,10 @@ void release(DpZero1& z) {
     DpComm& c = *z.comm;
     DeviceGuard g(c.device);
     cudaDeviceSynchronize();
-    if (z.zero1) soar_zero1_destroy(z.zero1);
+    for (void* h : z.zero1) soar_zero1_destroy(h);
+    z.zero1.clear();
     if (z.optim) soar_optim_destroy(z.optim);
-    z.zero1 = z.optim = nullptr;
+    z.optim = nullptr;
     for (void* p : z.peers) soar_ipc_close(p, c.device);
     z.peers.clear();
     barrier_on(c, c.stream);
@@ -185,6 +247,8 @@ void release(DpZero1& z) {
         if (p) soar_ipc_free(p, c.device);
         p = nullptr;
     }
+    for (void* p : z.extra) soar_ipc_free(p, c.device);
+    z.extra.clear();
     if (z.d_part) cudaFree(z.d_part);
     z.d_part = nullptr;
 }
@@ -287,15 +351,17 @@ SOAR_API int soar_dp_zero1_create(void* comm, uint64_t n_params, uint64_t bucket
     z->sync_mode = sync_mode;
     z->n = n_params;
     std::string why;
-    // 1. local buffers and their IPC handles
-    unsigned char handles[3][SOAR_IPC_HANDLE_BYTES];
+    // 1-2. local buffers, their IPC handles exchanged, the peers' opened
     const size_t bytes[3] = {2 * n_params, 2 * n_params, SOAR_ZERO1_SIGNAL_BYTES};
-    bool ok = true;
-    for (int k = 0; k < 3 && ok; ++k) {
-        ok = soar_ipc_alloc(bytes[k], c.device, &z->local[k], handles[k]) == SOAR_OK;
-        if (!ok) why = soar_last_error();
+    std::vector<void*> bases[3], locals;
+    bool ok = symmetric_alloc(*z, 3, bytes, bases, locals, &why);
+    for (size_t k = 0; k < locals.size(); ++k) z->local[k] = locals[k];
+    if (!ok) {
+        release(*z);
+        delete z;
+        return fail("soar_dp_zero1_create: " + why);
     }
-    if (ok && init_params &&
+    if (init_params &&
         cudaMemcpy(z->local[1], init_params, 2 * n_params, cudaMemcpyDefault) != cudaSuccess) {
         ok = false;
         why = "initial params copy failed";
@@ -309,53 +375,10 @@ SOAR_API int soar_dp_zero1_create(void* comm, uint64_t n_params, uint64_t bucket
         delete z;
         return fail("soar_dp_zero1_create: " + why);
     }
-    // 2. exchange the handles and open the peers' buffers
-    std::vector<unsigned char> all(static_cast<size_t>(c.world) * sizeof handles);
-    {
-        unsigned char* d_buf = nullptr;
-        cudaError_t e = cudaMalloc(&d_buf, all.size());
-        if (e == cudaSuccess)
-            e = cudaMemcpyAsync(d_buf + c.rank * sizeof handles, handles, sizeof handles,
-                                cudaMemcpyHostToDevice, c.stream);
-        ncclResult_t r = ncclSuccess;
-        if (e == cudaSuccess)
-            r = c.api->all_gather(d_buf + c.rank * sizeof handles, d_buf, sizeof handles,
-                                  ncclUint8, c.comm, c.stream);
-        if (e == cudaSuccess && r == ncclSuccess)
-            e = cudaMemcpyAsync(all.data(), d_buf, all.size(), cudaMemcpyDeviceToHost, c.stream);
-        if (e == cudaSuccess) e = cudaStreamSynchronize(c.stream);
-        if (d_buf) cudaFree(d_buf);
-        ok = e == cudaSuccess && r == ncclSuccess;
-        if (!ok) why = "handle exchange failed";
-    }
-    std::vector<void*> bases[3];
-    for (int k = 0; k < 3; ++k) bases[k].assign(c.world, nullptr);
-    for (int q = 0; q < c.world && ok; ++q) {
-        for (int k = 0; k < 3 && ok; ++k) {
-            if (q == c.rank) {
-                bases[k][q] = z->local[k];
-                continue;
-            }
-            const unsigned char* h = all.data() + (q * 3 + k) * SOAR_IPC_HANDLE_BYTES;
-            void* p = nullptr;
-            ok = soar_ipc_open(h, c.device, &p) == SOAR_OK;
-            if (ok) {
-                z->peers.push_back(p);
-                bases[k][q] = p;
-            } else {
-                why = soar_last_error();
-            }
-        }
-    }
-    if (!agree(c, ok, &why)) {
-        release(*z);
-        delete z;
-        return fail("soar_dp_zero1_create: " + why);
-    }
     // 3-4. the owned slices, the shard optimizer and the fused step's handle
     const std::vector<Bucket> plan = plan_buckets(n_params, bucket, c.world, c.rank);
     std::vector<soar_tensor_desc> descs;
-    std::vector<soar_zero1_shard> shards;
+    std::vector<soar_zero1_shard>& shards = z->shards;
     for (const Bucket& b : plan) {
         if (!b.own_size) continue;
         soar_tensor_desc d{};
@@ -369,12 +392,17 @@ SOAR_API int soar_dp_zero1_create(void* comm, uint64_t n_params, uint64_t bucket
     }
     ok = soar_optim_create(descs.data(), static_cast<int>(descs.size()), opts, &z->optim) ==
          SOAR_OK;
+    void* z1 = nullptr;
     if (ok)
         ok = soar_zero1_create(z->optim, c.rank, c.world, bases[0].data(), bases[1].data(),
-                               shards.data(), static_cast<int>(shards.size()), &z->zero1) ==
-             SOAR_OK;
+                               shards.data(), static_cast<int>(shards.size()), &z1) == SOAR_OK;
+    if (ok) {
+        z->zero1.push_back(z1);
+        z->grads.push_back(z->local[0]);
+        z->param_bases = bases[1];
+    }
     if (ok && sync_mode == SOAR_DP_SYNC_DEVICE)
-        ok = soar_zero1_set_signals(z->zero1, bases[2].data()) == SOAR_OK;
+        ok = soar_zero1_set_signals(z1, bases[2].data()) == SOAR_OK;
     if (!ok) why = soar_last_error();
     // 5. every rank's signal block is zeroed and bound before any rank steps
     if (!agree(c, ok, &why)) {
@@ -390,9 +418,9 @@ SOAR_API int soar_dp_zero1_get_info(void* handle, soar_dp_zero1_info* out) {
     if (!handle || !out) return fail("null argument");
     const auto& z = *static_cast<DpZero1*>(handle);
     out->params = z.local[1];
-    out->grads = z.local[0];
+    out->grads = z.grads[z.cur];
     out->optimizer = z.optim;
-    out->zero1 = z.zero1;
+    out->zero1 = z.zero1[z.cur];
     out->n_params = z.n;
     out->shard_params = z.shard;
     out->rank = z.comm->rank;
@@ -403,15 +431,80 @@ SOAR_API int soar_dp_zero1_get_info(void* handle, soar_dp_zero1_info* out) {
 SOAR_API int soar_dp_zero1_step(void* handle, void* stream) {
     if (!handle) return fail("null handle");
     auto& z = *static_cast<DpZero1*>(handle);
-    if (z.sync_mode == SOAR_DP_SYNC_DEVICE) return soar_zero1_step(z.zero1, stream);
+    void* z1 = z.zero1[z.cur];
+    if (z.sync_mode == SOAR_DP_SYNC_DEVICE) return soar_zero1_step(z1, stream);
     // synchronised by NCCL between the launches
     DpComm& c = *z.comm;
     int rc = soar_dp_barrier(&c, stream);                        // every rank's grads complete
-    if (rc == SOAR_OK) rc = soar_zero1_reduce_sumsq(z.zero1, z.d_part, stream);
+    if (rc == SOAR_OK) rc = soar_zero1_reduce_sumsq(z1, z.d_part, stream);
     if (rc == SOAR_OK) rc = soar_dp_allgather_f64(&c, z.d_part, z.d_part + 1, 1, stream);
-    if (rc == SOAR_OK) rc = soar_zero1_apply_allgather(z.zero1, z.d_part + 1, c.world, stream);
+    if (rc == SOAR_OK) rc = soar_zero1_apply_allgather(z1, z.d_part + 1, c.world, stream);
     if (rc == SOAR_OK) rc = soar_dp_barrier(&c, stream);         // peers' param writes landed
     return rc;
+}
+
+SOAR_API int soar_dp_zero1_add_grads(void* handle, int* out_index) {
+    if (!handle || !out_index) return fail("null argument");
+    auto& z = *static_cast<DpZero1*>(handle);
+    DpComm& c = *z.comm;
+    DeviceGuard g(c.device);
+    std::string why;
+    // a gradient buffer and a signal block of their own, symmetric
+    const size_t bytes[2] = {2 * z.n, SOAR_ZERO1_SIGNAL_BYTES};
+    std::vector<void*> bases[2];
+    if (!symmetric_alloc(z, 2, bytes, bases, z.extra, &why))
+        return fail("soar_dp_zero1_add_grads: " + why);
+    void* gbuf = bases[0][c.rank];
+    // the shard optimizer reads the owned slices of the new buffer as a
+    // gradient set of its own; the new fused-step handle is bound while that
+    // set is in use (it checks the optimizer's slices against the buffer)
+    std::vector<void*> slices;
+    for (const soar_zero1_shard& s : z.shards)
+        slices.push_back(static_cast<uint16_t*>(gbuf) + s.offset);
+    int set = -1;
+    void* z1 = nullptr;
+    bool ok = soar_optim_add_grads(z.optim, slices.data(), &set) == SOAR_OK &&
+              set == static_cast<int>(z.zero1.size()) &&
+              soar_optim_use_grads(z.optim, set) == SOAR_OK;
+    if (ok)
+        ok = soar_zero1_create(z.optim, c.rank, c.world, bases[0].data(), z.param_bases.data(),
+                               z.shards.data(), static_cast<int>(z.shards.size()), &z1) ==
+             SOAR_OK;
+    if (ok && z.sync_mode == SOAR_DP_SYNC_DEVICE)
+        ok = soar_zero1_set_signals(z1, bases[1].data()) == SOAR_OK;
+    if (!ok) why = soar_last_error();
+    soar_optim_use_grads(z.optim, z.cur);
+    // every rank's new signal block is bound before any rank steps on it, and
+    // the set exists on every rank or on none (an unused optimizer gradient
+    // set and the buffers stay until destroy)
+    if (!agree(c, ok, &why)) {
+        if (z1) soar_zero1_destroy(z1);
+        return fail("soar_dp_zero1_add_grads: " + why);
+    }
+    z.zero1.push_back(z1);
+    z.grads.push_back(gbuf);
+    *out_index = static_cast<int>(z.zero1.size()) - 1;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_dp_zero1_use_grads(void* handle, int index) {
+    if (!handle) return fail("null handle");
+    auto& z = *static_cast<DpZero1*>(handle);
+    if (index < 0 || index >= static_cast<int>(z.zero1.size()))
+        return fail("bad gradient buffer index");
+    const int rc = soar_optim_use_grads(z.optim, index);
+    if (rc != SOAR_OK) return rc;
+    z.cur = index;
+    return SOAR_OK;
+}
+
+SOAR_API int soar_dp_zero1_grads(void* handle, int index, void** out_grads) {
+    if (!handle || !out_grads) return fail("null argument");
+    const auto& z = *static_cast<DpZero1*>(handle);
+    if (index < 0 || index >= static_cast<int>(z.grads.size()))
+        return fail("bad gradient buffer index");
+    *out_grads = z.grads[index];
+    return SOAR_OK;
 }
 
 SOAR_API int soar_dp_zero1_destroy(void* handle) {

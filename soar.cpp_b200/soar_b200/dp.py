@@ -275,11 +275,44 @@ class FusedZeroOneAdamW:
         self.shard_grads = [self.grads[b.own_start:b.own_start + b.own_size] for b in mine]
         self.opt = _o.AdamW.borrow(info.optimizer, [b.own_size for b in mine], self.device)
         self.zero1 = C.c_void_p(info.zero1)
+        self.grad_buffers = [self.grads]
+        self._mine = mine
         self.part = torch.zeros(1, dtype=torch.float64, device=dev)
         self.parts = torch.zeros(self.world, dtype=torch.float64, device=dev)
 
     def _stream(self):
         return self.torch.cuda.current_stream().cuda_stream
+
+    def add_grads(self) -> int:
+        """Collective: another symmetric gradient buffer (soar_dp_zero1_add_grads),
+        so the next step's gradient can be written while a step reads the
+        current one. Returns its index; its view is grad_buffers[index]."""
+        import ctypes as C
+
+        from . import optim as _o
+        k = C.c_int()
+        _o._check(self.lib.soar_dp_zero1_add_grads(self.handle, C.byref(k)),
+                  "soar_dp_zero1_add_grads")
+        ptr = C.c_void_p()
+        _o._check(self.lib.soar_dp_zero1_grads(self.handle, k.value, C.byref(ptr)),
+                  "soar_dp_zero1_grads")
+        self.grad_buffers.append(self.torch.as_tensor(
+            _DevView(ptr.value, self.n, "<i2"), device=f"cuda:{self.device}").view(
+            self.torch.bfloat16))
+        return k.value
+
+    def use_grads(self, index: int) -> None:
+        """The gradient buffer the next steps reduce (every rank the same)."""
+        import ctypes as C
+
+        from . import optim as _o
+        _o._check(self.lib.soar_dp_zero1_use_grads(self.handle, index), "soar_dp_zero1_use_grads")
+        info = _o.DpZero1Info()
+        _o._check(self.lib.soar_dp_zero1_get_info(self.handle, C.byref(info)),
+                  "soar_dp_zero1_get_info")
+        self.zero1 = C.c_void_p(info.zero1)
+        self.grads = self.grad_buffers[index]
+        self.shard_grads = [self.grads[b.own_start:b.own_start + b.own_size] for b in self._mine]
 
     def barrier(self):
         """Stream-ordered barrier: completes on this GPU only after every

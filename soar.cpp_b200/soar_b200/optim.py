@@ -131,6 +131,9 @@ SIGNATURES: dict[str, tuple] = {
                                        C.c_void_p, C.c_int, C.POINTER(C.c_void_p)]),
     "soar_dp_zero1_get_info": (C.c_int, [C.c_void_p, C.c_void_p]),
     "soar_dp_zero1_step": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "soar_dp_zero1_add_grads": (C.c_int, [C.c_void_p, C.POINTER(C.c_int)]),
+    "soar_dp_zero1_use_grads": (C.c_int, [C.c_void_p, C.c_int]),
+    "soar_dp_zero1_grads": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_void_p)]),
     "soar_dp_zero1_destroy": (C.c_int, [C.c_void_p]),
     "soar_optim_add_grads": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p), C.POINTER(C.c_int)]),
     "soar_optim_use_grads": (C.c_int, [C.c_void_p, C.c_int]),

@@ -5,7 +5,8 @@
 //   test_dp_gpu <rank> <world> <id file> <output prefix> [device|nccl]
 //
 // Rank 0 writes NCCL's unique id to <id file>; the other ranks read it there.
-// Every rank steps 5 times on its own seeded bf16 gradient (loss scale 1024,
+// Every rank adds a second gradient buffer and the steps alternate between
+// the two. Every rank steps 5 times on its own seeded bf16 gradient (loss scale 1024,
 // growth every 2 clean steps, clip 1.0; +inf in rank 1's gradient at step 3,
 // so that step is skipped everywhere) and writes its parameter buffer to
 // <prefix>.rank<r>. Rank 0 also runs the same 5 steps as a single-GPU
@@ -156,6 +157,10 @@ int main(int argc, char** argv) {
         ext.growth_interval = 2;
         ext.device = rank;
         soar::optim::ZeroOneAdamW z(comm, kN, kBucket, opts, ext, p0.data(), sync);
+        // a second gradient buffer: the steps alternate between the two
+        const int second = z.add_grads();
+        CHECK(second == 1 && z.grads(0) != z.grads(1), "second gradient buffer (index %d)",
+              second);
 
         // rank 0's single-GPU optimizer on the rank-averaged gradient
         uint16_t *ref_p = nullptr, *ref_g = nullptr;
@@ -174,6 +179,7 @@ int main(int argc, char** argv) {
         const float inv_r = 1.0f / static_cast<float>(world);
         for (int t = 1; t <= kSteps; ++t) {
             const std::vector<uint16_t> g = grads_of(rank, t, scale);
+            z.use_grads((t - 1) % 2);
             cudaMemcpy(z.grads(), g.data(), kN * 2, cudaMemcpyHostToDevice);
             z.step();
             mine.push_back(z.info());

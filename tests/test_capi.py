@@ -101,6 +101,10 @@ def test_data_parallel_bootstrap_rejects_bad_arguments():
     assert lib.soar_dp_zero1_destroy(None) == -1
     info = optim.DpZero1Info()
     assert lib.soar_dp_zero1_get_info(None, ctypes.byref(info)) == -1
+    k = ctypes.c_int()
+    assert lib.soar_dp_zero1_add_grads(None, ctypes.byref(k)) == -1
+    assert lib.soar_dp_zero1_use_grads(None, 0) == -1
+    assert lib.soar_dp_zero1_grads(None, 0, ctypes.byref(out)) == -1
 
 
 def test_bench_probe_is_a_separate_library_and_checks_arguments():
