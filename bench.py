@@ -503,13 +503,16 @@ def run_ours(args):
     torch.cuda.synchronize()
     e2e_ms, e2e_copies = e2e_overlapped(torch, z.step, stream, grad_bufs, use_set, params,
                                         g_pin, p_pin, own, args.e2e_steps)
+    barrier()
+    torch.cuda.synchronize()
+    pcie_ms = pcie_floor(torch, stream, grad_bufs[0], g_pin, params, p_pin, own)
     if use_set is not None:
         use_set(0)
         del grad_bufs, grads2
-    t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+    t = torch.tensor([e2e_ms, pcie_ms], dtype=torch.float64, device=dev)
     if comm:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    e2e_ms = float(t[0])
+    e2e_ms, pcie_ms = float(t[0]), float(t[1])
 
     # ---- parity of one more step: oracle replay on rank 0, identity on all --
     barrier()
@@ -608,7 +611,12 @@ def run_ours(args):
                                               "while step s runs" if world == 1 or fused
                                               else ""),
                 "steps": args.e2e_steps, "ms_per_step": e2e_ms / args.e2e_steps,
-                "copies": e2e_copies},
+                "copies": e2e_copies,
+                "roofline": {"bound": "pcie", "floor_ms_per_step": pcie_ms,
+                             "frac": pcie_ms / (e2e_ms / args.e2e_steps),
+                             "floor": "the same H2D and D2H bytes as one step, both directions "
+                                      "at once on two copy streams, no step (all ranks at "
+                                      "once), max over ranks"}},
         "clocks": clock_info,
         "gpu_launches": launches_per_step * args.steps,
         "phases_ms": phases,
@@ -682,6 +690,30 @@ def e2e_overlapped(torch, step, stream, grad_bufs, use_set, params, g_pin, p_pin
               "d2h_gbs": round(gb_back / (d2h_ms * 1e-3), 1), "grad_buffers": nb}
     del snaps
     return e0.elapsed_time(e1), copies
+
+
+def pcie_floor(torch, stream, dst, g_pin, src, p_pin, own, reps=3) -> float:
+    """The PCIe floor of one end-to-end step: the step's upload (g_pin ->
+    dst) and read-back (src's owned slices -> p_pin) on two copy streams at
+    once, with no step, `reps` times; ms per repetition on `stream`."""
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    h2d.wait_event(e0)
+    d2h.wait_event(e0)
+    for _ in range(reps):
+        with torch.cuda.stream(h2d):
+            dst.copy_(g_pin, non_blocking=True)
+        with torch.cuda.stream(d2h):
+            for lo, sz in own:
+                p_pin[lo:lo + sz].copy_(src[lo:lo + sz], non_blocking=True)
+    for s in (h2d, d2h):
+        done = torch.cuda.Event()
+        done.record(s)
+        stream.wait_event(done)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
 
 
 def parity_check(torch, np, z, world, rank, comm, g_pin, grads, params) -> dict:
