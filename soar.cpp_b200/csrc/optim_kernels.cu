@@ -345,6 +345,7 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
         ApplyArgs a, AgArgs ag) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int kStages = apply_stages(kMixed, kEma, kSgd);
+    static_assert(!kAg || kStages >= kAgStoreLag + 2, "stages held by store reads");
     __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages];
     __shared__ StepCoeffs s_k;
     __shared__ int s_skip, s_found, s_err, s_drain_err;
@@ -467,6 +468,10 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
         } else {
             // ---- consumers ---------------------------------------------------
             const uint32_t tid = threadIdx.x;
+            // (all-gather) thread 0's store groups still reading their stage:
+            // the tiles q-ag_np+1 .. q, consecutive, since a tile without
+            // stores releases them all
+            int ag_np = 0;
             // Tile q (stage data already waited for). ok: compute it; stop:
             // the sequence ends here (stop marker or a failed wait). Returns
             // false when the consumers must leave the loop.
@@ -555,7 +560,27 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                                     bulk_store(ag.peer_param_base[qq] + off, src, kGradBytes * lv);
                         }
                         bulk_commit();
+                        if constexpr (kAg && kAgStoreLag > 0) {
+                            // Peer stores read their tile out of shared memory at
+                            // the link's pace. The stage is released kAgStoreLag
+                            // tiles later, so those reads overlap the math of the
+                            // next tiles instead of holding thread 0 (and with it
+                            // every consumer) at this tile.
+                            bulk_wait_read<kAgStoreLag>();
+                            if (ag_np == kAgStoreLag)
+                                mbar_arrive(smem_u32(&empty_bar[(q - kAgStoreLag) % kStages]));
+                            else
+                                ++ag_np;
+                            return true;
+                        }
                         bulk_wait_read_all();  // the stage may be refilled after this
+                    } else if constexpr (kAg && kAgStoreLag > 0) {
+                        if (ag_np) {
+                            bulk_wait_read_all();
+                            for (int j = 1; j <= ag_np; ++j)
+                                mbar_arrive(smem_u32(&empty_bar[(q - j) % kStages]));
+                            ag_np = 0;
+                        }
                     }
                     mbar_arrive(smem_u32(&empty_bar[s]));
                 }

@@ -134,6 +134,13 @@ constexpr int kTile = 1024;
 constexpr int kMaxStages = 6;
 constexpr int kConsumerWarps = 12;
 constexpr int kApplyThreads = (kConsumerWarps + 1) * 32;
+// Update kernel with the fused all-gather: tiles whose stores may still be
+// reading their stage while the consumers move on (0: every tile waits for
+// its own stores' reads before the next).
+#ifndef SOAR_AG_STORE_LAG
+#define SOAR_AG_STORE_LAG 2
+#endif
+constexpr int kAgStoreLag = SOAR_AG_STORE_LAG;
 // bytes of one pipeline stage: grad tile + master, m, v (AdamW) or master,
 // momentum (SGD) tiles, + the EMA shadow tile
 __host__ __device__ constexpr size_t stage_bytes(bool mixed, bool ema = false, bool sgd = false) {
@@ -145,6 +152,8 @@ __host__ __device__ constexpr int apply_stages(bool mixed, bool ema = false, boo
                ? static_cast<int>(110592 / stage_bytes(mixed, ema, sgd))
                : kMaxStages;
 }
+static_assert(kAgStoreLag >= 0 && kAgStoreLag + 2 <= kMaxStages,
+              "the producer keeps at least two stages of loads ahead");
 __host__ __device__ constexpr size_t apply_smem_bytes(bool mixed, bool ema = false,
                                                       bool sgd = false) {
     return stage_bytes(mixed, ema, sgd) * apply_stages(mixed, ema, sgd);

@@ -96,6 +96,11 @@ __device__ __forceinline__ void bulk_wait_read_all() {
     asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// all but the newest N committed groups have finished reading shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
 
 // System-scope release store / acquire load (peer flags over NVLink).
 __device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
