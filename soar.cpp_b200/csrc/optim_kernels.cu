@@ -344,8 +344,12 @@ __global__ void __launch_bounds__(kApplyThreads, 2)
 k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restrict__ ctl,
         ApplyArgs a, AgArgs ag) {
     extern __shared__ __align__(128) unsigned char smem[];
-    constexpr int kStages = apply_stages(kMixed, kEma, kSgd);
+    constexpr int kStages = apply_stages(kMixed, kEma, kSgd, kAg);
     static_assert(!kAg || kStages >= kAgStoreLag + 2, "stages held by store reads");
+    // bf16 params of the all-gather leave through the push area (see kAgPushTiles)
+    constexpr bool kPushBuf = kMixed && kAg && kAgPushTiles > 0;
+    constexpr uint32_t kPushHalf = static_cast<uint32_t>(kAgPushTiles) * kTile * 2u;
+    constexpr uint32_t kPusher = 32;  // the consumer thread that issues those pushes
     __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages];
     __shared__ StepCoeffs s_k;
     __shared__ int s_skip, s_found, s_err, s_drain_err;
@@ -472,6 +476,10 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
             // the tiles q-ag_np+1 .. q, consecutive, since a tile without
             // stores releases them all
             int ag_np = 0;
+            // (push area) every consumer follows the same tile sequence: the
+            // open group's next slot and its half of the push area
+            uint32_t pb_slot = 0, pb_half = 0;
+            const uint32_t push_base = smem_u32(smem + kStages * kStage);
             // Tile q (stage data already waited for). ok: compute it; stop:
             // the sequence ends here (stop marker or a failed wait). Returns
             // false when the consumers must leave the loop.
@@ -480,6 +488,15 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                 const uint32_t s = q % kStages;
                 const uint32_t lv = len & ~(kVecElems - 1);
                 unsigned char* st = smem + s * kStage;
+                // (push area) a group is up to kAgPushTiles consecutive tiles of
+                // one chunk, all full but the last; it closes at the chunk's
+                // last tile, at a partial tile, or when it is full
+                const bool pb_close = ok && (lv < static_cast<uint32_t>(kTile) ||
+                                             t0 + kTile >= ch.n ||
+                                             pb_slot + 1 == static_cast<uint32_t>(kAgPushTiles));
+                const bool pb_data = pb_slot > 0 || lv > 0;  // the closing group holds params
+                uint2* pb_out = reinterpret_cast<uint2*>(
+                    smem + kStages * kStage + pb_half * kPushHalf + pb_slot * (kTile * 2u));
                 if (ok) {
                     const float lr_wd = __fmul_rn(a.lr, ch.wd);
                     const bool has_wd = ch.wd != 0.0f;
@@ -524,32 +541,62 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                             se[i] = e;
                         }
                         if constexpr (kMixed) {
-                            // the bf16 params take the grad's place in the stage
+                            // the bf16 params take the grad's place in the stage,
+                            // or their slot of the push area
                             uint2 p;
                             p.x = pack_bf16x2_rn(th.x, th.y);
                             p.y = pack_bf16x2_rn(th.z, th.w);
-                            reinterpret_cast<uint2*>(st)[i] = p;
+                            if constexpr (kPushBuf)
+                                pb_out[i] = p;
+                            else
+                                reinterpret_cast<uint2*>(st)[i] = p;
                         }
                     }
                     // the < 16-byte tail of the tile, straight from global memory
                     apply_scalar<kMixed, kAg, kEma, kSgd>(ch, t0 + lv, t0 + len, tid,
                                                           kConsumers, a, k, lr_wd, has_wd, ag);
                 }
+                if constexpr (kPushBuf) {
+                    // The next group writes the other half of the push area: the
+                    // pushes of the group before this one must have read it. They
+                    // left kAgPushTiles tiles ago, so this rarely waits.
+                    if (tid == kPusher && pb_close && pb_data) bulk_wait_read_all();
+                }
                 // make the stage's generic-proxy writes visible to the bulk store;
                 // after the barrier every consumer reads the same failure flag
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 consumers_sync<kConsumers>();
                 if (s_cfail[q & 1] || stop) return false;
+                if constexpr (kPushBuf) {
+                    if (pb_close) {
+                        if (tid == kPusher && pb_data) {
+                            // the group's params: into the local buffer and every peer
+                            const uint32_t first = t0 - pb_slot * kTile;
+                            const uint32_t bytes = 2u * (pb_slot * kTile + lv);
+                            const uint32_t src = push_base + pb_half * kPushHalf;
+                            bulk_store(static_cast<uint16_t*>(ch.param) + first, src, bytes);
+                            const size_t off = static_cast<const char*>(ch.param) -
+                                               ag.local_param_base + 2u * static_cast<size_t>(first);
+                            for (int qq = 0; qq < ag.world; ++qq)
+                                if (qq != ag.rank) bulk_store(ag.peer_param_base[qq] + off, src, bytes);
+                            bulk_commit();
+                        }
+                        if (pb_data) pb_half ^= 1u;
+                        pb_slot = 0;
+                    } else {
+                        ++pb_slot;
+                    }
+                }
                 if (tid == 0) {
                     if (lv) {
                         const uint32_t base = smem_u32(st);
-                        if constexpr (kMixed)
+                        if constexpr (kMixed && !kPushBuf)
                             bulk_store(static_cast<uint16_t*>(ch.param) + t0, base, 2u * lv);
                         bulk_store(ch.master + t0, base + kOffMaster, 4u * lv);
                         if (use_m) bulk_store(ch.m + t0, base + kOffM, 4u * lv);
                         if constexpr (!kSgd) bulk_store(ch.v + t0, base + kOffV, 4u * lv);
                         if constexpr (kEma) bulk_store(ch.m + a.ema_delta + t0, base + kOffE, 4u * lv);
-                        if constexpr (kAg) {
+                        if constexpr (kAg && !kPushBuf) {
                             // the fused all-gather: the same param tile into every peer
                             const size_t off = static_cast<const char*>(ch.param) -
                                                ag.local_param_base +
@@ -607,7 +654,7 @@ k_apply(const Chunk* __restrict__ chunks, int n_chunks, int n_vec, Ctl* __restri
                     return tile(ch, t0, len, q, ok, !ok);
                 });
             }
-            if (tid == 0) bulk_wait_all();
+            if (tid == 0 || (kPushBuf && tid == kPusher)) bulk_wait_all();
             // scalar chunks (misaligned heads, mixed-phase tensors)
             for (int c = s_err ? n_chunks : n_vec + static_cast<int>(blockIdx.x); c < n_chunks; c += gridDim.x) {
                 const Chunk ch = chunks[c];
@@ -866,15 +913,15 @@ template <bool kMixed, bool kAg, bool kEma, bool kSgd, bool kDyn>
 static cudaError_t set_smem_attr() {
     return cudaFuncSetAttribute(k_apply<kMixed, kAg, kEma, kSgd, kDyn>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                static_cast<int>(apply_smem_bytes(kMixed, kEma, kSgd)));
+                                static_cast<int>(apply_smem_bytes(kMixed, kEma, kSgd, kAg)));
 }
 
 template <bool kMixed, bool kAg, bool kEma, bool kSgd, bool kDyn>
 static void launch_apply_t(const Chunk* chunks, int n_chunks, int n_vec, Ctl* ctl,
                            const ApplyArgs& args, int grid, cudaStream_t stream, const AgArgs& ag) {
     launch_pdl(k_apply<kMixed, kAg, kEma, kSgd, kDyn>, dim3(grid), dim3(kApplyThreads),
-               apply_smem_bytes(kMixed, kEma, kSgd), stream, chunks, n_chunks, n_vec, ctl, args,
-               ag);
+               apply_smem_bytes(kMixed, kEma, kSgd, kAg), stream, chunks, n_chunks, n_vec, ctl,
+               args, ag);
 }
 
 // The 32 instantiations, indexed by (mixed, ag, ema, sgd, dyn) bits.

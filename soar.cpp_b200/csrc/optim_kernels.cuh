@@ -146,17 +146,31 @@ constexpr int kAgStoreLag = SOAR_AG_STORE_LAG;
 __host__ __device__ constexpr size_t stage_bytes(bool mixed, bool ema = false, bool sgd = false) {
     return (mixed ? 2u : 4u) * kTile + (sgd ? 8u : 12u) * kTile + (ema ? 4u : 0u) * kTile;
 }
-// stages that keep two CTAs per SM (<= ~108 KB of ring each)
-__host__ __device__ constexpr int apply_stages(bool mixed, bool ema = false, bool sgd = false) {
-    return static_cast<int>(110592 / stage_bytes(mixed, ema, sgd)) < kMaxStages
-               ? static_cast<int>(110592 / stage_bytes(mixed, ema, sgd))
+// Update kernel with the fused all-gather, bf16 params: the updated params of
+// this many consecutive tiles of one chunk leave in one push per peer (from a
+// double-buffered push area in shared memory, beside the ring); 0: every tile
+// pushes its own params from its stage.
+#ifndef SOAR_AG_PUSH_TILES
+#define SOAR_AG_PUSH_TILES 8
+#endif
+constexpr int kAgPushTiles = SOAR_AG_PUSH_TILES;
+__host__ __device__ constexpr size_t push_bytes(bool mixed, bool ag) {
+    return mixed && ag && kAgPushTiles > 0 ? 2u * kAgPushTiles * kTile * 2u : 0u;
+}
+// stages that keep two CTAs per SM (<= ~108 KB of ring and push area each)
+__host__ __device__ constexpr int apply_stages(bool mixed, bool ema = false, bool sgd = false,
+                                               bool ag = false) {
+    return static_cast<int>((110592 - push_bytes(mixed, ag)) / stage_bytes(mixed, ema, sgd)) <
+                   kMaxStages
+               ? static_cast<int>((110592 - push_bytes(mixed, ag)) / stage_bytes(mixed, ema, sgd))
                : kMaxStages;
 }
 static_assert(kAgStoreLag >= 0 && kAgStoreLag + 2 <= kMaxStages,
               "the producer keeps at least two stages of loads ahead");
 __host__ __device__ constexpr size_t apply_smem_bytes(bool mixed, bool ema = false,
-                                                      bool sgd = false) {
-    return stage_bytes(mixed, ema, sgd) * apply_stages(mixed, ema, sgd);
+                                                      bool sgd = false, bool ag = false) {
+    return stage_bytes(mixed, ema, sgd) * apply_stages(mixed, ema, sgd, ag) +
+           push_bytes(mixed, ag);
 }
 
 // Register-fed update for short lists (k_apply_direct): up to kDirectMaxRuns
