@@ -66,8 +66,8 @@ APPLY_TRAFFIC_BYTES = {200_000_000: 5_541_141_760}
 # launches of each kernel averaged). With every rank's buffers on one GPU, a
 # kernel's DRAM bytes are the per-GPU HBM bytes of its multi-GPU launch; the
 # writes that are still in L2 when the kernel ends are not in the count.
-DP_TRAFFIC_PER_ELEM = {8: {"k_rs_sumsq": (100_074_688 + 1_360_544) / 6_250_000,
-                           "k_apply<all-gather>": (87_747_232 + 122_004_608) / 6_250_000}}
+DP_TRAFFIC_PER_ELEM = {8: {"k_rs_sumsq": (100_074_400 + 1_204_672) / 6_250_000,
+                           "k_apply<all-gather>": (87_755_008 + 123_064_736) / 6_250_000}}
 # NVLink references of this pool (per direction per GPU): the measured peer
 # copy and NVLink 5's specification.
 NVLINK_PEER_COPY_GBS = 770.0

@@ -13,7 +13,10 @@ rounding -- 1/3 is inexact, so R = 3 pins the rounding); all R parameter
 buffers end identical; the step sequence, skip and loss scale match the
 single-process oracle run on the average gradient, with params within 1 bf16
 ulp. Ragged shards (N not divisible by R) and a 16-byte-misaligned bucket
-size are included."""
+size are included. One case (two ranks, 19,461 elements each) ends each
+rank's vector run with a tile of fewer than 8 elements after three full ones,
+so a group of updated params leaves for the peers closed by a tile that has no
+vector part."""
 import ctypes as C
 
 import numpy as np
@@ -33,28 +36,36 @@ STEPS = 4
 INF_STEP = 2
 
 
-def _grads(rank, step, scale):
-    g = synth.normal(synth.seed_of(60, rank, step), N, 0.01) * np.float32(scale)
+def _grads(rank, step, scale, n=N):
+    g = synth.normal(synth.seed_of(60, rank, step), n, 0.01) * np.float32(scale)
     if step == INF_STEP and rank == 0:
         g[77] = np.inf
     return synth.to_bf16_bits(g.astype(np.float32))
 
 
-@pytest.mark.parametrize("world", [3, 4, 8])
-def test_zero1_kernels_emulated_world(oracle_mod, cuda, world):
+@pytest.mark.parametrize("world,n,bucket", [(3, N, BUCKET), (4, N, BUCKET), (8, N, BUCKET),
+                                            (2, 2 * 19_461, 2 * 19_461)],
+                         ids=["w3", "w4", "w8", "w2-short-tail"])
+def test_zero1_kernels_emulated_world(oracle_mod, cuda, world, n, bucket):
     torch = cuda
     lib = _o.lib()
     bf = lambda a: torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).cuda()
     bits = lambda t: t.view(torch.int16).cpu().numpy().view(np.uint16).copy()
-    p0 = synth.to_bf16_bits(synth.normal(synth.seed_of(61), N, 0.02))
-    grads = [torch.empty(N, dtype=torch.bfloat16, device="cuda") for _ in range(world)]
+    p0 = synth.to_bf16_bits(synth.normal(synth.seed_of(61), n, 0.02))
+    def aligned_empty(count):
+        # a view starting on a 2048-byte boundary: where the chunk planner's
+        # tile boundaries fall is then fixed by the shard offsets alone
+        buf = torch.empty(count + 1024, dtype=torch.bfloat16, device="cuda")
+        off = (-buf.data_ptr() % 2048) // 2
+        return buf[off:off + count]
+    grads = [aligned_empty(n) for _ in range(world)]
     params = [bf(p0) for _ in range(world)]
     gb = (C.c_void_p * world)(*[g.data_ptr() for g in grads])
     pb = (C.c_void_p * world)(*[p.data_ptr() for p in params])
     scaler = sb.LossScalerOptions(init_scale=1024.0, growth_interval=2)
     opts, handles, plans = [], [], []
     for r in range(world):
-        plan = [b for b in dp.plan_buckets(N, BUCKET, world, r) if b.own_size > 0]
+        plan = [b for b in dp.plan_buckets(n, bucket, world, r) if b.own_size > 0]
         opt = sb.AdamW([sb.ParamGroup([params[r][b.own_start:b.own_start + b.own_size]
                                        for b in plan], 0.01)],
                        layout="bf16_mixed", max_grad_norm=1.0, loss_scaler=scaler,
@@ -71,7 +82,7 @@ def test_zero1_kernels_emulated_world(oracle_mod, cuda, world):
     part = torch.zeros(world, dtype=torch.float64, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
 
-    full = dp.plan_buckets(N, BUCKET, 1, 0)
+    full = dp.plan_buckets(n, bucket, 1, 0)
     ref = oracle_mod.PortOptimizer([p0[b.start:b.start + b.size] for b in full],
                                    [0.01] * len(full),
                                    oracle_mod.StepConfig(layout=1, max_norm=1.0, use_scaler=True,
@@ -80,7 +91,7 @@ def test_zero1_kernels_emulated_world(oracle_mod, cuda, world):
     scale = 1024.0
     try:
         for t in range(1, STEPS + 1):
-            ins = [_grads(r, t, scale) for r in range(world)]
+            ins = [_grads(r, t, scale, n) for r in range(world)]
             for r in range(world):
                 grads[r].copy_(bf(ins[r]))
             for r in range(world):   # every rank's reduce-scatter + partial
