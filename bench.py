@@ -72,6 +72,8 @@ DP_TRAFFIC_PER_ELEM = {8: {"k_rs_sumsq": (100_074_400 + 1_204_672) / 6_250_000,
 # copy and NVLink 5's specification.
 NVLINK_PEER_COPY_GBS = 770.0
 NVLINK_SPEC_GBS = 900.0
+# B200 HBM3e specification (DGX figure), reported beside the measured copy peak
+HBM_SPEC_GBS = 8000.0
 L2_FLUSH_BYTES = 256 << 20    # twice the 126 MB L2
 
 
@@ -564,6 +566,7 @@ def run_ours(args):
     achieved = apply_bytes / (apply_ms_max * 1e-3) / 1e9
     hbm = {"bound": "hbm", "kernel": "k_apply", "achieved": achieved, "peak": peak,
            "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+           "peak_spec": HBM_SPEC_GBS, "frac_spec": achieved / HBM_SPEC_GBS,
            "traffic": APPLY_TRAFFIC_BYTES.get(shard_params),
            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one k_apply "
                              "launch of this command at N=1" if shard_params in
