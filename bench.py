@@ -629,6 +629,8 @@ def run_ours(args):
     }
     if world > 1:
         line["rooflines"] = per_kernel
+        line["composite_roofline"] = composite_roofline(world, n, shard_params,
+                                                        ms_max / args.steps, peak)
         line["nvlink_probe"] = probe
     if configs is not None:
         line["configs"] = configs
@@ -852,6 +854,38 @@ def parity_check(torch, np, z, world, rank, comm, g_pin, grads, params) -> dict:
     except Exception as ex:  # reported, never a reason to lose the bench line
         out["error"] = f"{type(ex).__name__}: {str(ex)[:300]}"
     return out
+
+
+def composite_roofline(world, n, shard_params, step_ms, hbm_peak) -> dict:
+    """The whole data-parallel step against the sum of its two phases' floors
+    (the phases cannot overlap: the global norm decides the clip between them).
+    Each phase's floor is its binding resource, as in dp_rooflines:
+      reduce-scatter  max((R+1) x shard x 2 B / HBM, (R-1) x shard x 2 B / NVLink)
+      update + AG     max((28 x shard + (R-1) x shard x 2 B) / HBM,
+                          (R-1) x shard x 2 B / NVLink)
+    with NVLink bytes per rank and direction. `additive` is the sum of the
+    shard update at the HBM peak and both collectives at the NVLink peak: no
+    lower bound here, since the fused kernels overlap the two (at 2 GPUs the
+    step runs below it). Measured peaks (HBM copy, peer copy) and the
+    specifications (8 TB/s HBM, 900 GB/s NVLink per direction)."""
+    nvl = (world - 1) * shard_params * 2
+    upd = BYTES_PER_PARAM * shard_params
+
+    def floors(hbm, link):
+        rs = max((world + 1) * shard_params * 2 / hbm, nvl / link)
+        ag = max((upd + nvl) / hbm, nvl / link)
+        return (rs + ag) * 1e3 / 1e9, (upd / hbm + 2 * nvl / link) * 1e3 / 1e9
+
+    f, add = floors(hbm_peak, NVLINK_PEER_COPY_GBS)
+    fs, adds = floors(HBM_SPEC_GBS, NVLINK_SPEC_GBS)
+    return {"floor": "per phase, the slower of HBM and NVLink; summed over reduce-scatter and "
+                     "update + all-gather",
+            "params": n, "floor_ms": round(f, 4), "frac": f / step_ms,
+            "floor_ms_spec": round(fs, 4), "frac_spec": fs / step_ms,
+            "peaks": {"hbm": hbm_peak, "nvlink": NVLINK_PEER_COPY_GBS},
+            "peaks_spec": {"hbm": HBM_SPEC_GBS, "nvlink": NVLINK_SPEC_GBS},
+            "additive": {"formula": "28 B x N/R / HBM + 2 x (R-1)/R x 2 B x N / NVLink",
+                         "ms": round(add, 4), "ms_spec": round(adds, 4)}}
 
 
 def dp_rooflines(world, shard_params, phases, hbm_peak) -> tuple[dict, dict]:

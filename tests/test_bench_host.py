@@ -135,3 +135,18 @@ def test_dp_rooflines_are_recomputable_from_the_phases():
     assert both2["k_rs_sumsq"]["bound"] == "nvlink"
     assert dom2["bound"] == "hbm" and dom2["kernel"] == "k_apply<all-gather>"
     assert dom2["bytes_per_launch"] == 28 * 100_000_000 + 200_000_000
+
+
+def test_composite_roofline_is_a_lower_bound_of_the_phases():
+    # 8 GPUs: both phases NVLink-bound, so the floor is 2 x 350 MB at the link rate
+    c = bench.composite_roofline(8, 200_000_000, 25_000_000, 1.153, 6552.0)
+    assert abs(c["floor_ms"] - 2 * 350e6 / (bench.NVLINK_PEER_COPY_GBS * 1e9) * 1e3) < 1e-3
+    assert abs(c["frac"] - c["floor_ms"] / 1.153) < 1e-3
+    assert c["floor_ms"] <= c["additive"]["ms"] and c["floor_ms_spec"] < c["floor_ms"]
+    # 2 GPUs: the update phase is HBM-bound; the per-phase floor stays below the
+    # measured step where the additive form (no overlap) would exceed it
+    c2 = bench.composite_roofline(2, 200_000_000, 100_000_000, 0.834, 6552.0)
+    rs = 200e6 / (bench.NVLINK_PEER_COPY_GBS * 1e9)
+    ag = (28 * 100e6 + 200e6) / (6552.0 * 1e9)
+    assert abs(c2["floor_ms"] - (rs + ag) * 1e3) < 1e-3
+    assert c2["frac"] < 1.0 < c2["additive"]["ms"] / 0.834
