@@ -100,7 +100,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--params", type=int, default=N_PARAMS)
-    ap.add_argument("--e2e-steps", type=int, default=20)
+    # 40: the pipeline's fill and drain (the first upload and the last
+    # read-back run alone) amortise to ~0.2 ms of a ~9 ms step
+    ap.add_argument("--e2e-steps", type=int, default=40)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-configs", action="store_true",
                     help="leave the configs key out of the N=1 line")
