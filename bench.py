@@ -935,9 +935,9 @@ def dp_rooflines(world, shard_params, phases, hbm_peak) -> tuple[dict, dict]:
             out[k]["traffic_source"] = ("HBM bytes per launch: one-GPU ncu capture of the "
                                         f"{world} ranks' kernels (--emulate-world {world}, "
                                         "shard 6.25M), scaled to this shard; compare hbm_bytes")
-        if bound == "nvlink":
-            out[k]["peak_spec"] = NVLINK_SPEC_GBS
-            out[k]["frac_spec"] = achieved / NVLINK_SPEC_GBS
+        spec = NVLINK_SPEC_GBS if bound == "nvlink" else HBM_SPEC_GBS
+        out[k]["peak_spec"] = spec
+        out[k]["frac_spec"] = achieved / spec
         if not fused:
             out[k]["kernel"] += " (NCCL around it)"
     dominant = max(out.values(), key=lambda r: r["ms"])

@@ -135,6 +135,7 @@ def test_dp_rooflines_are_recomputable_from_the_phases():
     assert both2["k_rs_sumsq"]["bound"] == "nvlink"
     assert dom2["bound"] == "hbm" and dom2["kernel"] == "k_apply<all-gather>"
     assert dom2["bytes_per_launch"] == 28 * 100_000_000 + 200_000_000
+    assert abs(dom2["frac_spec"] - dom2["achieved"] / bench.HBM_SPEC_GBS) < 1e-12
 
 
 def test_composite_roofline_is_a_lower_bound_of_the_phases():
