@@ -86,10 +86,17 @@ struct DeviceGuard {
     }
 };
 
-constexpr int kRsTile = 2048;           // bf16 elements per tile (4 KB per rank)
+#ifndef SOAR_RS_TILE
+#define SOAR_RS_TILE 2048
+#endif
+#ifndef SOAR_RS_SMEM_KB
+#define SOAR_RS_SMEM_KB 96
+#endif
+constexpr int kRsTile = SOAR_RS_TILE;   // bf16 elements per tile (4 KB per rank)
 constexpr int kRsConsumerWarps = 8;     // 256 consumer threads, 8 elements each per tile
 constexpr int kRsThreads = (kRsConsumerWarps + 1) * 32;
-constexpr size_t kRsSmemBudget = 96 * 1024;
+constexpr size_t kRsSmemBudget = SOAR_RS_SMEM_KB * 1024;  // ring of stages, per CTA
+static_assert(kRsTile % 8 == 0 && kRsSmemBudget <= 200 * 1024, "reduce-scatter ring shape");
 
 // One contiguous run of an owned slice: element offset in the flat buffers.
 struct __align__(16) RsChunk {
